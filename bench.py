@@ -1,0 +1,298 @@
+"""Benchmark of the Swin3D backbone hot path on B200.
+
+Default (what the driver runs): the era5-shape Swin3D U-net backbone forward (
+embed 512, encoder depths (6,10,8) / decoder (8,10,6), heads (8,16,32)/(32,16,8), window (2,6,12),
+latent grid (4,180,360), batch 1) in the ``bf16_mixed`` tier, random init ~N(0, 0.02), synthetic
+~N(0,1) input. One step = one backbone forward. Metric: ms/step (lower is better).
+
+* ``value``      device time per step with the input resident in HBM (CUDA events, max over ranks).
+* ``e2e``        the same step through the public API from pinned host memory: H2D of the input,
+                 backbone, D2H of the full output, all inside the timed region.
+* ``roofline``   the window-attention kernel (the hot kernel of this library), from CUDA events
+                 around every attention launch inside the timed region: algorithmic bytes
+                 (Q, K, V read + O written, bf16) / kernel time, against the measured HBM peak.
+* ``cpu_baseline`` the CPU oracle (upstream FP32 algorithm restated in torch-CPU) on one shifted
+                 block per stage, extrapolated to the 48-block step (rank 0, N = 1 only).
+
+Multi-GPU (``torchrun --nproc-per-node N``): every rank runs its own backbone step on its own
+input (independent ensemble members, no data-path collective): weak scaling, replicas.
+
+``--impl reference`` times the reference algorithm on the host CPU instead (the CPU oracle, see
+above; rank 0 only) and prints the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "era5 Swin3D backbone ms/step (bf16_mixed)"
+UNIT = "ms/step"
+CONFIG4 = dict(embed_dim=512, encoder_depths=(6, 10, 8), encoder_num_heads=(8, 16, 32),
+               decoder_depths=(8, 10, 6), decoder_num_heads=(32, 16, 8), window_size=(2, 6, 12))
+PATCH_RES = (4, 180, 360)
+STAGES = [((4, 180, 360), 512, 8, 12), ((4, 90, 180), 1024, 16, 20), ((4, 45, 90), 2048, 32, 16)]
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int) -> None:
+        self.proc = None
+        ident = str(device_index)
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            pass
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", ident,
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws > 1:
+        import torch.distributed as dist
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        return dist, dist.get_rank(), ws, local
+    return None, 0, 1, 0
+
+
+def _max_over_ranks(dist, v: float) -> float:
+    if dist is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(dist):
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ----------------------------------------------------------------------------------------------
+# CPU baseline: the upstream FP32 block algorithm restated on CPU (oracle), one shifted block per
+# stage, extrapolated by block count.
+# ----------------------------------------------------------------------------------------------
+def _cpu_block_ms(res, dim, heads, seed):
+    from oracle import block as OB
+    from tests._inputs import block_param_shapes, init_params
+    g = torch.Generator().manual_seed(seed)
+    C, H, W = res
+    x = torch.randn(1, C * H * W, dim, generator=g)
+    c = torch.randn(1, 512, generator=g)
+    shapes = block_param_shapes(dim, 512)
+    p = init_params(shapes, seed=seed + 1)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        OB.block_forward(x, c, res, p, num_heads=heads, window_size=(2, 6, 12), shift_size=(1, 3, 6))
+    return (time.perf_counter() - t0) * 1e3
+
+
+def cpu_baseline_sample() -> dict:
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    per = [_cpu_block_ms(res, dim, heads, 7 + i) for i, (res, dim, heads, _) in enumerate(STAGES)]
+    total = sum(t * n for t, (_, _, _, n) in zip(per, STAGES))
+    return {"value": round(total, 1), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": ("one shifted block per stage (S1 (4,180,360)x512, S2 (4,90,180)x1024, S3 (4,45,90)x2048) "
+                       f"timed once each [{', '.join(f'{t:.0f}' for t in per)} ms], x(12,20,16) blocks; "
+                       "stage merges/splits (1.4% of FLOPs) not timed")}
+
+
+def run_reference(args) -> None:
+    dist, rank, world, _ = (None, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), 0)
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    times = {0: [], 1: [], 2: []}
+    for i in range(args.warmup + args.steps):
+        s = i % 3
+        res, dim, heads, _ = STAGES[s]
+        ms = _cpu_block_ms(res, dim, heads, 7 + s)
+        if i >= args.warmup:
+            times[s].append(ms)
+    for s in times:
+        if not times[s]:
+            res, dim, heads, _ = STAGES[s]
+            times[s].append(_cpu_block_ms(res, dim, heads, 7 + s))
+    value = sum(statistics.mean(times[s]) * STAGES[s][3] for s in range(3))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 1), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config4: era5 Swin3D backbone forward, 48 blocks, grid (4,180,360), batch 1",
+                   "parallelism": "host CPU"},
+        "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": "each step = one shifted block of stage S1/S2/S3 in turn on the CPU oracle "
+                                   "(upstream FP32 algorithm), mean per stage x (12,20,16) blocks"},
+        "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------------------------
+# B200 arm
+# ----------------------------------------------------------------------------------------------
+def run_b200(args) -> None:
+    from flash_aurora_b200 import window_attn as WA
+    from flash_aurora_b200.swin3d import Swin3DTransformerBackbone, init_random_weights_
+
+    dist, rank, world, local = _dist()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    model = Swin3DTransformerBackbone(**CONFIG4, precision="bf16_mixed").to(dev).eval()
+    init_random_weights_(model, generator=gen)
+    C, H, W = PATCH_RES
+    L = C * H * W
+    x = torch.randn(1, L, CONFIG4["embed_dim"], device=dev, generator=gen)
+    lead = timedelta(hours=6)
+
+    def step(inp):
+        return model(inp, lead_time=lead, rollout_step=0, patch_res=PATCH_RES)
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            y = step(x)
+        _barrier(dist)
+        # Device-resident timing.
+        rec = WA.KernelRecorder()
+        WA.set_recorder(rec)
+        sampler = ClockSampler(local)
+        _barrier(dist)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            y = step(x)
+        e1.record()
+        _barrier(dist)
+        clocks = sampler.stop()
+        WA.set_recorder(None)
+        ms = e0.elapsed_time(e1) / args.steps
+        ms = _max_over_ranks(dist, ms)
+        attn_ms, attn_bytes, attn_flops, attn_launches = rec.totals()
+
+        # End to end from pinned host memory through the public API.
+        x_host = x.cpu().pin_memory()
+        out_host = torch.empty(tuple(y.shape), dtype=y.dtype, pin_memory=True)
+        x_dev = torch.empty_like(x)
+        _barrier(dist)
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record()
+        for _ in range(args.steps):
+            x_dev.copy_(x_host, non_blocking=True)
+            yy = step(x_dev)
+            out_host.copy_(yy, non_blocking=True)
+        e3.record()
+        _barrier(dist)
+        e2e_ms = _max_over_ranks(dist, e2.elapsed_time(e3) / args.steps)
+
+    hbm, _, peak_kind = _peaks()
+    achieved = attn_bytes / (attn_ms * 1e-3) / 1e9 if attn_ms > 0 else 0.0
+    per_step_launches = 4 * sum(CONFIG4["encoder_depths"]) + 4 * sum(CONFIG4["decoder_depths"])
+    line = {
+        "metric": METRIC, "value": round(ms, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config4: era5 Swin3D U-net backbone forward (embed 512, depths (6,10,8)/(8,10,6), "
+                               "heads (8,16,32)/(32,16,8), window (2,6,12), grid (4,180,360), batch 1), bf16_mixed",
+                   "global_batch": world, "parallelism": f"replicas x{world} (independent members, no collective)",
+                   "l2": "inputs and per-block activations > L2 (126 MB)"},
+        "e2e": {"value": round(e2e_ms, 2), "unit": UNIT, "h2d_bytes_per_step": x.numel() * x.element_size(),
+                "d2h_bytes_per_step": y.numel() * y.element_size()},
+        "gpu_launches": per_step_launches * args.steps,
+        "roofline": {"kernel": "window attention (bf16, per-launch average over the timed region)",
+                     "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 3), "traffic": None, "peak_kind": peak_kind,
+                     "tflops": round(attn_flops / (attn_ms * 1e-3) / 1e12, 1) if attn_ms > 0 else None,
+                     "launches": attn_launches, "kernel_ms_per_step": round(attn_ms / args.steps, 3)},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,55 @@
+"""flash_aurora_b200: the Aurora Swin3D backbone block hot path on NVIDIA B200 (sm_100a).
+
+Hand-written CUDA kernels behind a C ABI (``include/flash_aurora_b200.h``,
+``libflash_aurora_b200.so`` built in-tree by ``python -m flash_aurora_b200.build``), with a
+PyTorch host layer that mirrors the operator interface of upstream Flash-Aurora:
+
+* ``swin3d_layout``  roll_pad_partition_windows / crop_roll_unmerge_windows
+                     (upstream ``ops/triton_swin3d_layout.py``)
+* ``adaln``          adaptive_layernorm_film_forward / ..._add_residual_forward
+                     (upstream ``ops/triton_adaln.py``)
+* ``window_attn``    WinAttnPrecision, window_attn_fwd_cute, window_attn_fwd_cute_qkvpacked,
+                     window_attn_dispatch (upstream ``ops/cute/window_attn_fwd.py``)
+* ``swin3d``         Swin3DTransformerBlock / Swin3DTransformerBackbone with upstream state-dict
+                     keys (upstream ``aurora/model/swin3d.py``, ``film.py``)
+* ``sharding``       latitude-band window sharding with a point-to-point halo exchange
+"""
+
+from .adaln import (
+    adaptive_layernorm_film_add_residual_forward,
+    adaptive_layernorm_film_forward,
+    unmerge_adaptive_layernorm_film_add_residual,
+)
+from .swin3d_layout import (
+    crop_roll_unmerge_windows,
+    crop_roll_unmerge_windows_triton,
+    roll_pad_partition_windows,
+    roll_pad_partition_windows_triton,
+)
+from .util import maybe_adjust_windows, window_geometry
+from .window_attn import (
+    WinAttnPrecision,
+    shifted_window_group_ids,
+    window_attn_dispatch,
+    window_attn_fwd_cute,
+    window_attn_fwd_cute_qkvpacked,
+)
+from .workspace_pool import InferenceWorkspacePool
+
+__all__ = [
+    "adaptive_layernorm_film_add_residual_forward",
+    "adaptive_layernorm_film_forward",
+    "unmerge_adaptive_layernorm_film_add_residual",
+    "crop_roll_unmerge_windows",
+    "crop_roll_unmerge_windows_triton",
+    "roll_pad_partition_windows",
+    "roll_pad_partition_windows_triton",
+    "maybe_adjust_windows",
+    "window_geometry",
+    "WinAttnPrecision",
+    "shifted_window_group_ids",
+    "window_attn_dispatch",
+    "window_attn_fwd_cute",
+    "window_attn_fwd_cute_qkvpacked",
+    "InferenceWorkspacePool",
+]

@@ -1,0 +1,147 @@
+"""Fused AdaLN (LayerNorm without affine + FiLM modulation) with optional residual add.
+
+Drop-in for upstream ``flash_aurora/aurora/ops/triton_adaln.py``: same function names,
+arguments, output dtypes and ``ValueError`` cases (CUDA, float32/bfloat16, ``D <= 2048``,
+residual/x dtype rules, shapes). Extensions used by the block: ``out_bf16`` (a second, bfloat16
+copy of the output for the next BF16 GEMM) and the unmerge-fused variant that reads the
+AdaLN input straight from attention windows.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .util import window_geometry
+
+__all__ = [
+    "adaptive_layernorm_film_forward",
+    "adaptive_layernorm_film_add_residual_forward",
+    "unmerge_adaptive_layernorm_film_add_residual",
+]
+
+_MAX_D = 2048
+_DTYPES = (torch.float32, torch.bfloat16)
+
+
+def _mod_rows(t: torch.Tensor, B: int, D: int, name: str) -> torch.Tensor:
+    if tuple(t.shape) not in ((B, 1, D), (B, D)):
+        raise ValueError(f"{name} must have shape (B, 1, D) = {(B, 1, D)}, got {tuple(t.shape)}")
+    if t.dtype not in _DTYPES:
+        raise ValueError(f"{name} must be float32 or bfloat16")
+    return t.reshape(B, D).contiguous()
+
+
+def _launch(x, residual, scale, shift, scale_bias, eps, out, out_bf16, B, L, D, what):
+    rc = _lib.load().fa_adaln_film(
+        x.data_ptr(), _lib.dtype_code(x.dtype),
+        residual.data_ptr() if residual is not None else None,
+        _lib.dtype_code(residual.dtype) if residual is not None else 0,
+        scale.data_ptr(), shift.data_ptr(), _lib.dtype_code(scale.dtype),
+        float(scale_bias), float(eps), out.data_ptr(), _lib.dtype_code(out.dtype),
+        out_bf16.data_ptr() if out_bf16 is not None else None, B, L, D, _lib.stream_ptr(x.device))
+    _lib.check(rc, what)
+
+
+def adaptive_layernorm_film_forward(
+    x: torch.Tensor,
+    scale: torch.Tensor,
+    shift: torch.Tensor,
+    scale_bias: float,
+    eps: float = 1e-5,
+    *,
+    output_fp32: bool = False,
+) -> torch.Tensor:
+    """``LN(x) * (scale_bias + scale) + shift`` (upstream triton_adaln.py:33-80)."""
+    if x.device.type != "cuda" or x.dtype not in _DTYPES:
+        raise ValueError("adaptive_layernorm_film_forward requires CUDA float32/bfloat16 x.")
+    B, L, D = x.shape
+    if D > _MAX_D:
+        raise ValueError(f"adaptive_layernorm_film_forward supports D <= {_MAX_D} for now.")
+    scale = _mod_rows(scale, B, D, "scale")
+    shift = _mod_rows(shift, B, D, "shift").to(scale.dtype)
+    out = torch.empty(B, L, D, device=x.device, dtype=torch.float32 if output_fp32 else x.dtype)
+    _launch(x.contiguous(), None, scale, shift, scale_bias, eps, out, None, B, L, D,
+            "adaptive_layernorm_film_forward")
+    return out
+
+
+def adaptive_layernorm_film_add_residual_forward(
+    residual: torch.Tensor,
+    x: torch.Tensor,
+    scale: torch.Tensor,
+    shift: torch.Tensor,
+    scale_bias: float,
+    eps: float = 1e-5,
+    *,
+    output_fp32: bool = False,
+    out: Optional[torch.Tensor] = None,
+    out_bf16: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """``residual + LN(x) * (scale_bias + scale) + shift`` (upstream triton_adaln.py:83-145)."""
+    if residual.device.type != "cuda" or x.device.type != "cuda":
+        raise ValueError("adaptive_layernorm_film_add_residual_forward requires CUDA tensors.")
+    if residual.dtype not in _DTYPES or x.dtype not in _DTYPES:
+        raise ValueError("adaptive_layernorm_film_add_residual_forward requires float32/bfloat16.")
+    if not output_fp32 and residual.dtype != x.dtype:
+        raise ValueError("residual and x must have the same dtype unless output_fp32=True.")
+    if output_fp32 and residual.dtype != torch.float32:
+        raise ValueError("output_fp32=True requires residual.dtype == float32.")
+    if residual.shape != x.shape:
+        raise ValueError("residual and x must have the same shape.")
+    B, L, D = x.shape
+    if D > _MAX_D:
+        raise ValueError(f"adaptive_layernorm_film_add_residual_forward supports D <= {_MAX_D}.")
+    scale = _mod_rows(scale, B, D, "scale")
+    shift = _mod_rows(shift, B, D, "shift").to(scale.dtype)
+    out_dtype = torch.float32 if output_fp32 else x.dtype
+    if out is None:
+        out = torch.empty(B, L, D, device=x.device, dtype=out_dtype)
+    _launch(x.contiguous(), residual.contiguous(), scale, shift, scale_bias, eps, out, out_bf16, B, L, D,
+            "adaptive_layernorm_film_add_residual_forward")
+    return out
+
+
+def unmerge_adaptive_layernorm_film_add_residual(
+    windows: torch.Tensor,
+    residual: torch.Tensor,
+    scale: torch.Tensor,
+    shift: torch.Tensor,
+    res: tuple[int, int, int],
+    window_size: tuple[int, int, int],
+    shift_size: tuple[int, int, int],
+    scale_bias: float = 0.0,
+    eps: float = 1e-5,
+    *,
+    out_bf16: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """``residual + AdaLN(crop_roll_unmerge(windows))`` in one pass, fp32 output.
+
+    Replaces the upstream pair ``crop_roll_unmerge_windows_triton`` + ``norm1.forward_add_residual``
+    (swin3d.py:751-800, film.py:101-139): the merged branch tensor is never materialised.
+    """
+    for t, n in ((windows, "windows"), (residual, "residual")):
+        _lib.require_cuda(t, "unmerge_adaptive_layernorm_film_add_residual")
+    if windows.dtype not in _DTYPES or residual.dtype != torch.float32:
+        raise ValueError("windows must be float32/bfloat16 and residual float32")
+    C, H, W = res
+    B, L, D = residual.shape
+    if L != C * H * W:
+        raise ValueError(f"residual has {L} tokens, res {tuple(res)} has {C * H * W}")
+    if D > _MAX_D:
+        raise ValueError(f"AdaLN supports D <= {_MAX_D}")
+    _, _, _, _, nW, N = window_geometry(tuple(res), tuple(window_size), tuple(shift_size))
+    if tuple(windows.shape) != (B * nW, N, D):
+        raise ValueError(f"windows must have shape {(B * nW, N, D)}, got {tuple(windows.shape)}")
+    scale = _mod_rows(scale, B, D, "scale")
+    shift = _mod_rows(shift, B, D, "shift").to(scale.dtype)
+    out = torch.empty(B, L, D, device=residual.device, dtype=torch.float32)
+    rc = _lib.load().fa_unmerge_adaln_film(
+        windows.contiguous().data_ptr(), _lib.dtype_code(windows.dtype), residual.contiguous().data_ptr(),
+        _lib.FA_F32, scale.data_ptr(), shift.data_ptr(), _lib.dtype_code(scale.dtype), float(scale_bias),
+        float(eps), out.data_ptr(), _lib.FA_F32, out_bf16.data_ptr() if out_bf16 is not None else None,
+        B, C, H, W, D, _lib.i32x3(window_size), _lib.i32x3(shift_size), _lib.stream_ptr(residual.device))
+    _lib.check(rc, "unmerge_adaptive_layernorm_film_add_residual")
+    return out

@@ -1,0 +1,219 @@
+// Fused AdaLN (LayerNorm without affine + FiLM modulation) + residual add (sm_100a).
+//
+//   out = [residual +] LN(x) * (scale_bias + scale[b]) + shift[b]
+//
+// One warp per token row. The row is read from HBM once into registers; mean and variance are
+// two-pass (sum, then sum of squared deviations) with warp-shuffle reductions, all in fp32.
+// The upstream Triton kernel (ops/triton_adaln.py:148-203) reads x twice and uses
+// E[x^2] - mean^2; the two-pass form matches PyTorch's LayerNorm more closely.
+//
+// The gather variant reads the LN input row of token (c, h, w) directly from the attention
+// windows (crop + inverse roll + merge), fusing crop_roll_unmerge into norm1.
+#include "fa_common.cuh"
+
+namespace fa {
+namespace {
+
+constexpr int kWarpsPerBlock = 8;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void load8_any(const T* p, float v[8], bool stream) {
+  if (stream) Vec8<T>::load_stream(p, v); else Vec8<T>::load(p, v);
+}
+
+__device__ __forceinline__ void load_mod8(const void* p, bool bf16, int64_t off, float v[8]) {
+  if (bf16) Vec8<__nv_bfloat16>::load(reinterpret_cast<const __nv_bfloat16*>(p) + off, v);
+  else Vec8<float>::load(reinterpret_cast<const float*>(p) + off, v);
+}
+
+__device__ __forceinline__ float load_mod1(const void* p, bool bf16, int64_t off) {
+  return bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[off])
+              : reinterpret_cast<const float*>(p)[off];
+}
+
+struct AdaArgs {
+  const void* x;
+  const void* residual;  // same dtype as out, or null
+  const void* scale;
+  const void* shift;
+  bool mod_bf16;
+  float scale_bias, eps;
+  void* out;
+  __nv_bfloat16* out_bf16;  // optional copy
+  int64_t B, L;
+  int32_t D;
+  bool gather;
+  LayoutParams lp;
+};
+
+// kChunks = number of 8-element (vector path) or 1-element (scalar path) chunks per lane.
+template <typename TX, typename TO, bool kVec, int kChunks>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) adaln_kernel(AdaArgs a) {
+  constexpr int kE = kVec ? 8 : 1;  // elements per chunk per lane
+  const int lane = threadIdx.x & 31;
+  const int D = a.D;
+  const int64_t rows = a.B * a.L;
+  const TX* __restrict__ xg = reinterpret_cast<const TX*>(a.x);
+  const TO* __restrict__ rg = reinterpret_cast<const TO*>(a.residual);
+  TO* __restrict__ og = reinterpret_cast<TO*>(a.out);
+  const float inv_d = 1.0f / (float)D;
+
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kWarpsPerBlock) {
+    const int64_t b = row / a.L;
+    int64_t xrow = row;
+    if (a.gather) {
+      const int32_t t = (int32_t)(row - b * a.L);
+      const int32_t w = t % a.lp.W;
+      const int32_t h = (t / a.lp.W) % a.lp.H;
+      const int32_t c = t / (a.lp.W * a.lp.H);
+      xrow = b * (int64_t)a.lp.nW * a.lp.N + unmerge_slot(a.lp, c, h, w);
+    }
+    const TX* xr = xg + xrow * D;
+    float v[kChunks][kE];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+      const int col = (i * 32 + lane) * kE;
+      if (col < D) {
+        if constexpr (kVec) load8_any(xr + col, v[i], true);
+        else v[i][0] = to_f32(xr[col]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < kE; ++e) v[i][e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < kE; ++e) s += v[i][e];
+    }
+    const float mean = warp_sum(s) * inv_d;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+      const int col = (i * 32 + lane) * kE;
+      if (col < D) {
+#pragma unroll
+        for (int e = 0; e < kE; ++e) {
+          const float d = v[i][e] - mean;
+          q += d * d;
+        }
+      }
+    }
+    const float rstd = rsqrtf(warp_sum(q) * inv_d + a.eps);
+    const int64_t mrow = b * D;
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+      const int col = (i * 32 + lane) * kE;
+      if (col >= D) continue;
+      float y[kE];
+      if constexpr (kVec) {
+        float sc[8], sh[8];
+        load_mod8(a.scale, a.mod_bf16, mrow + col, sc);
+        load_mod8(a.shift, a.mod_bf16, mrow + col, sh);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = (v[i][e] - mean) * rstd * (a.scale_bias + sc[e]) + sh[e];
+        if (rg) {
+          float r[8];
+          Vec8<TO>::load_stream(rg + row * D + col, r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) y[e] += r[e];
+        }
+        Vec8<TO>::store(og + row * D + col, y);
+        if (a.out_bf16) Vec8<__nv_bfloat16>::store(a.out_bf16 + row * D + col, y);
+      } else {
+        const float sc = load_mod1(a.scale, a.mod_bf16, mrow + col);
+        const float sh = load_mod1(a.shift, a.mod_bf16, mrow + col);
+        y[0] = (v[i][0] - mean) * rstd * (a.scale_bias + sc) + sh;
+        if (rg) y[0] += to_f32(rg[row * D + col]);
+        og[row * D + col] = from_f32<TO>(y[0]);
+        if (a.out_bf16) a.out_bf16[row * D + col] = __float2bfloat16_rn(y[0]);
+      }
+    }
+  }
+}
+
+template <typename TX, typename TO, bool kVec, int kChunks>
+int launch_adaln_chunks(const AdaArgs& a, cudaStream_t s) {
+  const int64_t rows = a.B * a.L;
+  if (rows == 0 || a.D == 0) return FA_OK;
+  int64_t blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  adaln_kernel<TX, TO, kVec, kChunks><<<(unsigned)blocks, kWarpsPerBlock * 32, 0, s>>>(a);
+  return check_launch("adaln_kernel");
+}
+
+template <typename TX, typename TO>
+int launch_adaln(const AdaArgs& a, bool vec, cudaStream_t s) {
+  if (vec) {
+    if (a.D <= 256) return launch_adaln_chunks<TX, TO, true, 1>(a, s);
+    if (a.D <= 512) return launch_adaln_chunks<TX, TO, true, 2>(a, s);
+    if (a.D <= 1024) return launch_adaln_chunks<TX, TO, true, 4>(a, s);
+    return launch_adaln_chunks<TX, TO, true, 8>(a, s);
+  }
+  if (a.D <= 256) return launch_adaln_chunks<TX, TO, false, 8>(a, s);
+  if (a.D <= 1024) return launch_adaln_chunks<TX, TO, false, 32>(a, s);
+  return launch_adaln_chunks<TX, TO, false, 64>(a, s);
+}
+
+int run_adaln(AdaArgs a, int x_dtype, int residual_dtype, int mod_dtype, int out_dtype,
+              cudaStream_t s) {
+  FA_REQUIRE(a.x && a.scale && a.shift && a.out, FA_ERR_INVALID, "null tensor pointer");
+  FA_REQUIRE(x_dtype == FA_F32 || x_dtype == FA_BF16, FA_ERR_INVALID, "x dtype must be FA_F32 or FA_BF16");
+  FA_REQUIRE(out_dtype == FA_F32 || out_dtype == FA_BF16, FA_ERR_INVALID, "out dtype must be FA_F32 or FA_BF16");
+  FA_REQUIRE(mod_dtype == FA_F32 || mod_dtype == FA_BF16, FA_ERR_INVALID, "scale/shift dtype must be FA_F32 or FA_BF16");
+  FA_REQUIRE(!a.residual || residual_dtype == out_dtype, FA_ERR_INVALID,
+             "residual dtype must equal the output dtype");
+  FA_REQUIRE(out_dtype == FA_F32 || x_dtype == FA_BF16, FA_ERR_INVALID,
+             "a bf16 output needs a bf16 input (fp32 input writes fp32)");
+  FA_REQUIRE(a.B >= 0 && a.L >= 0 && a.D >= 0, FA_ERR_INVALID, "negative size");
+  FA_REQUIRE(a.D <= 2048, FA_ERR_UNSUPPORTED, "AdaLN supports D <= 2048");
+  a.mod_bf16 = mod_dtype == FA_BF16;
+  const bool vec = (a.D % 8 == 0) && aligned16(a.x) && aligned16(a.scale) && aligned16(a.shift) &&
+                   aligned16(a.out) && (!a.residual || aligned16(a.residual)) &&
+                   (!a.out_bf16 || aligned16(a.out_bf16));
+  if (x_dtype == FA_F32) return launch_adaln<float, float>(a, vec, s);
+  if (out_dtype == FA_F32) return launch_adaln<__nv_bfloat16, float>(a, vec, s);
+  return launch_adaln<__nv_bfloat16, __nv_bfloat16>(a, vec, s);
+}
+
+}  // namespace
+}  // namespace fa
+
+using namespace fa;
+
+extern "C" int fa_adaln_film(const void* x, int x_dtype, const void* residual, int residual_dtype,
+                             const void* scale, const void* shift, int mod_dtype, float scale_bias,
+                             float eps, void* out, int out_dtype, void* out_bf16, int64_t B,
+                             int64_t L, int64_t D, void* stream) {
+  AdaArgs a{};
+  a.x = x; a.residual = residual; a.scale = scale; a.shift = shift;
+  a.scale_bias = scale_bias; a.eps = eps; a.out = out;
+  a.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);
+  a.B = B; a.L = L; a.D = (int32_t)D; a.gather = false;
+  FA_REQUIRE(D < (1 << 30), FA_ERR_INVALID, "D too large");
+  return run_adaln(a, x_dtype, residual_dtype, mod_dtype, out_dtype, (cudaStream_t)stream);
+}
+
+extern "C" int fa_unmerge_adaln_film(const void* windows, int windows_dtype, const void* residual,
+                                     int residual_dtype, const void* scale, const void* shift,
+                                     int mod_dtype, float scale_bias, float eps, void* out,
+                                     int out_dtype, void* out_bf16, int64_t B, int64_t C, int64_t H,
+                                     int64_t W, int64_t D, const int32_t window_size[3],
+                                     const int32_t shift_size[3], void* stream) {
+  Geometry g;
+  int rc = make_geometry(C, H, W, window_size, shift_size, &g);
+  if (rc != FA_OK) return rc;
+  FA_REQUIRE(D < (1 << 30), FA_ERR_INVALID, "D too large");
+  AdaArgs a{};
+  a.x = windows; a.residual = residual; a.scale = scale; a.shift = shift;
+  a.scale_bias = scale_bias; a.eps = eps; a.out = out;
+  a.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);
+  a.B = B; a.L = C * H * W; a.D = (int32_t)D; a.gather = true; a.lp = layout_params(g);
+  return run_adaln(a, windows_dtype, residual_dtype, mod_dtype, out_dtype, (cudaStream_t)stream);
+}

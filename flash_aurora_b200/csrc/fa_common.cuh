@@ -1,0 +1,187 @@
+// Shared helpers of the flash_aurora_b200 CUDA library (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "flash_aurora_b200.h"
+
+namespace fa {
+
+// ---------------------------------------------------------------------------------------------
+// Error reporting: every C-ABI entry point returns a status and records a thread-local message.
+// ---------------------------------------------------------------------------------------------
+int set_error(int code, const std::string& msg);
+int check_launch(const char* what);  // cudaGetLastError -> FA_ERR_CUDA with the kernel name
+
+#define FA_REQUIRE(cond, code, msg)                      \
+  do {                                                   \
+    if (!(cond)) return ::fa::set_error((code), (msg));  \
+  } while (0)
+
+#define FA_CUDA(call)                                                                         \
+  do {                                                                                        \
+    cudaError_t e__ = (call);                                                                 \
+    if (e__ != cudaSuccess)                                                                   \
+      return ::fa::set_error(FA_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e__)); \
+  } while (0)
+
+// ---------------------------------------------------------------------------------------------
+// Window geometry (upstream util.py:54-72 clamp, swin3d.py:415-432 padding split).
+// ---------------------------------------------------------------------------------------------
+struct Geometry {
+  int64_t C, H, W;
+  int32_t ws[3], ss[3], pf[3];  // window, shift (after clamp), front pads (C, H, W)
+  int64_t padded[3];
+  int64_t grid[3];  // windows per axis
+  int64_t nW;
+  int32_t N;
+};
+
+int make_geometry(int64_t C, int64_t H, int64_t W, const int32_t* window_size,
+                  const int32_t* shift_size, Geometry* g);
+
+// Device-side copy of the index parameters of a layout gather.
+struct LayoutParams {
+  int32_t C, H, W;
+  int32_t wc, wh, ww;
+  int32_t sc, sh, sw;
+  int32_t pc, ph, pw;  // front pads
+  int32_t W1, HW1;     // windows along W, windows per C slab
+  int32_t nW, N;
+};
+
+inline LayoutParams layout_params(const Geometry& g) {
+  LayoutParams p;
+  p.C = (int32_t)g.C; p.H = (int32_t)g.H; p.W = (int32_t)g.W;
+  p.wc = g.ws[0]; p.wh = g.ws[1]; p.ww = g.ws[2];
+  p.sc = g.ss[0]; p.sh = g.ss[1]; p.sw = g.ss[2];
+  p.pc = g.pf[0]; p.ph = g.pf[1]; p.pw = g.pf[2];
+  p.W1 = (int32_t)g.grid[2];
+  p.HW1 = (int32_t)(g.grid[1] * g.grid[2]);
+  p.nW = (int32_t)g.nW;
+  p.N = g.N;
+  return p;
+}
+
+// Source token (c*H + h)*W + w of window slot (win, n) of one batch element, or -1 for pad.
+// Same mapping as ops/triton_swin3d_layout.py:218-246.
+__device__ __forceinline__ int32_t partition_source(const LayoutParams& p, int32_t win, int32_t n) {
+  const int32_t c1 = win / p.HW1;
+  const int32_t r1 = win - c1 * p.HW1;
+  const int32_t h1 = r1 / p.W1;
+  const int32_t w1 = r1 - h1 * p.W1;
+  const int32_t whw = p.wh * p.ww;
+  const int32_t wc = n / whw;
+  const int32_t r2 = n - wc * whw;
+  const int32_t wh = r2 / p.ww;
+  const int32_t ww = r2 - wh * p.ww;
+  const int32_t cs = c1 * p.wc + wc - p.pc;
+  const int32_t hs = h1 * p.wh + wh - p.ph;
+  const int32_t wsv = w1 * p.ww + ww - p.pw;
+  if (cs < 0 || cs >= p.C || hs < 0 || hs >= p.H || wsv < 0 || wsv >= p.W) return -1;
+  int32_t xc = cs + p.sc; if (xc >= p.C) xc -= p.C;
+  int32_t xh = hs + p.sh; if (xh >= p.H) xh -= p.H;
+  int32_t xw = wsv + p.sw; if (xw >= p.W) xw -= p.W;
+  return (xc * p.H + xh) * p.W + xw;
+}
+
+// Window slot win*N + n holding token (c, h, w) of one batch element (triton_swin3d_layout.py:283-305).
+__device__ __forceinline__ int32_t unmerge_slot(const LayoutParams& p, int32_t c, int32_t h, int32_t w) {
+  int32_t cs = c - p.sc; if (cs < 0) cs += p.C;
+  int32_t hs = h - p.sh; if (hs < 0) hs += p.H;
+  int32_t wsv = w - p.sw; if (wsv < 0) wsv += p.W;
+  const int32_t pc = cs + p.pc, ph = hs + p.ph, pw = wsv + p.pw;
+  const int32_t c1 = pc / p.wc, wc = pc - c1 * p.wc;
+  const int32_t h1 = ph / p.wh, wh = ph - h1 * p.wh;
+  const int32_t w1 = pw / p.ww, ww = pw - w1 * p.ww;
+  const int32_t win = c1 * p.HW1 + h1 * p.W1 + w1;
+  const int32_t n = (wc * p.wh + wh) * p.ww + ww;
+  return win * p.N + n;
+}
+
+// ---------------------------------------------------------------------------------------------
+// 8-element vector I/O (16 B of bf16, 32 B of fp32) with conversion to/from fp32 registers.
+// ---------------------------------------------------------------------------------------------
+template <typename T> struct Vec8;
+
+template <> struct Vec8<float> {
+  static __device__ __forceinline__ void load(const float* p, float v[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  static __device__ __forceinline__ void load_stream(const float* p, float v[8]) {
+    const float4 a = __ldcs(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldcs(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  static __device__ __forceinline__ void store(float* p, const float v[8]) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  static __device__ __forceinline__ void zero(float* p) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    reinterpret_cast<float4*>(p)[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);  // round to nearest even
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
+  // bf16 -> fp32 is exact: the bf16 bits are the top half of the fp32 pattern.
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+
+template <> struct Vec8<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float v[8]) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+    float2 f;
+    f = unpack_bf16x2(a.x); v[0] = f.x; v[1] = f.y;
+    f = unpack_bf16x2(a.y); v[2] = f.x; v[3] = f.y;
+    f = unpack_bf16x2(a.z); v[4] = f.x; v[5] = f.y;
+    f = unpack_bf16x2(a.w); v[6] = f.x; v[7] = f.y;
+  }
+  static __device__ __forceinline__ void load_stream(const __nv_bfloat16* p, float v[8]) {
+    const uint4 a = __ldcs(reinterpret_cast<const uint4*>(p));
+    float2 f;
+    f = unpack_bf16x2(a.x); v[0] = f.x; v[1] = f.y;
+    f = unpack_bf16x2(a.y); v[2] = f.x; v[3] = f.y;
+    f = unpack_bf16x2(a.z); v[4] = f.x; v[5] = f.y;
+    f = unpack_bf16x2(a.w); v[6] = f.x; v[7] = f.y;
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, const float v[8]) {
+    uint4 a;
+    a.x = pack_bf16x2(v[0], v[1]);
+    a.y = pack_bf16x2(v[2], v[3]);
+    a.z = pack_bf16x2(v[4], v[5]);
+    a.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(p) = a;
+  }
+  static __device__ __forceinline__ void zero(__nv_bfloat16* p) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(0u, 0u, 0u, 0u);
+  }
+};
+
+// Scalar element access for the unaligned fallback paths.
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int num_sms();  // SM count of the current device (cached per device)
+
+}  // namespace fa

@@ -1,0 +1,151 @@
+/*
+ * flash_aurora_b200 — C ABI of the B200 (sm_100a) Swin3D backbone block hot path.
+ *
+ * One shared library (libflash_aurora_b200.so) exports these entry points. They take plain
+ * device pointers, sizes and a CUDA stream (cudaStream_t passed as void*), launch
+ * asynchronously on that stream, never allocate device memory, never synchronise, and return
+ * an int status (FA_OK = 0, negative on error; fa_last_error() describes the last failure of
+ * the calling thread). Nothing here aborts the process.
+ *
+ * Each entry point replaces one call site of the upstream Flash-Aurora Python/Triton/CuTe-DSL
+ * implementation; the citation is given beside it (paths relative to that project).
+ */
+#ifndef FLASH_AURORA_B200_H
+#define FLASH_AURORA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types. */
+enum { FA_F32 = 0, FA_BF16 = 1 };
+
+/* Status codes. */
+enum {
+  FA_OK = 0,
+  FA_ERR_INVALID = -1,     /* bad argument: null pointer, shape, stride, alignment, dtype */
+  FA_ERR_UNSUPPORTED = -2, /* valid but not implemented here (e.g. head_dim != 64) */
+  FA_ERR_CUDA = -3,        /* a CUDA runtime/driver call failed; message has the CUDA error */
+  FA_ERR_TIMEOUT = -4      /* a bounded device-side wait gave up (see fa_attention_status) */
+};
+
+/* Window-attention precision (upstream WinAttnPrecision, ops/cute/window_attn_fwd.py:49-60). */
+enum {
+  FA_ATTN_BF16 = 0,        /* bf16 in/out, fp32 accumulation and softmax */
+  FA_ATTN_FP32_3XTF32 = 1  /* fp32 in/out, 3xTF32 split products, fp32 softmax */
+};
+
+/* Attention output layouts (upstream output_layout "bhnd" / "bnc", window_attn_fwd.py:246-255). */
+enum { FA_LAYOUT_BHND = 0, FA_LAYOUT_BNC = 1 };
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* fa_last_error(void);
+
+/* ABI version of this library (major * 100 + minor). */
+int fa_version(void);
+
+/*
+ * Window geometry of one block call: window/shift after the clamp of
+ * flash_aurora/aurora/model/util.py:54-72, the front pads (C front, H top, W left) of the
+ * symmetric zero padding (swin3d.py:415-432), the padded extents, the window count
+ * nW = (Cp/wc)(Hp/wh)(Wp/ww) and the tokens per window N = wc*wh*ww
+ * (ops/triton_swin3d_layout.py:78-88). Host-only.
+ */
+int fa_window_geometry(int64_t C, int64_t H, int64_t W, const int32_t window_size[3],
+                       const int32_t shift_size[3], int32_t ws_out[3], int32_t ss_out[3],
+                       int32_t pad_front_out[3], int64_t padded_out[3], int64_t* num_windows_out,
+                       int32_t* window_tokens_out);
+
+/*
+ * Fused cyclic shift (roll by -ss) + zero pad + 3D window partition:
+ * x (B, C, H, W, D) -> windows (B*nW, N, D). Replaces roll_pad_partition_windows_triton
+ * (ops/triton_swin3d_layout.py:58-121, kernel :192-250). x_dtype/windows_dtype are FA_F32 or
+ * FA_BF16 (an f32 -> bf16 store rounds to nearest even; bf16 -> f32 is exact). Bit-exact
+ * gather: every output element is an input element or +0.
+ */
+int fa_roll_pad_partition(const void* x, int x_dtype, void* windows, int windows_dtype,
+                          int64_t B, int64_t C, int64_t H, int64_t W, int64_t D,
+                          const int32_t window_size[3], const int32_t shift_size[3], void* stream);
+
+/*
+ * Inverse: windows (B*nW, N, D) -> out (B, C, H, W, D), reading only non-pad tokens.
+ * Replaces crop_roll_unmerge_windows_triton (ops/triton_swin3d_layout.py:124-189, kernel
+ * :253-307).
+ */
+int fa_crop_roll_unmerge(const void* windows, int windows_dtype, void* out, int out_dtype,
+                         int64_t B, int64_t C, int64_t H, int64_t W, int64_t D,
+                         const int32_t window_size[3], const int32_t shift_size[3], void* stream);
+
+/*
+ * Fused AdaLN: out = [residual +] LN(x) * (scale_bias + scale) + shift, LN without affine,
+ * statistics in fp32 from a single read of x. x: (B, L, D) f32|bf16; residual: (B, L, D) or
+ * NULL; scale/shift: (B, D) rows (mod_dtype f32|bf16); out: (B, L, D) in out_dtype; out_bf16:
+ * optional second copy of out rounded to bf16 (NULL to skip). D <= 2048. Replaces
+ * adaptive_layernorm_film_forward / adaptive_layernorm_film_add_residual_forward
+ * (ops/triton_adaln.py:33-145, kernel :148-203; module film.py:72-139).
+ */
+int fa_adaln_film(const void* x, int x_dtype, const void* residual, int residual_dtype,
+                  const void* scale, const void* shift, int mod_dtype, float scale_bias, float eps,
+                  void* out, int out_dtype, void* out_bf16, int64_t B, int64_t L, int64_t D,
+                  void* stream);
+
+/*
+ * crop_roll_unmerge fused into the AdaLN above: the AdaLN input row of token (c, h, w) is read
+ * straight from the attention windows (B*nW, N, D), so the merged branch tensor is never
+ * written. Replaces the pair swin3d.py:751-756 (unmerge) + film.py:101-139 (norm1).
+ */
+int fa_unmerge_adaln_film(const void* windows, int windows_dtype, const void* residual,
+                          int residual_dtype, const void* scale, const void* shift, int mod_dtype,
+                          float scale_bias, float eps, void* out, int out_dtype, void* out_bf16,
+                          int64_t B, int64_t C, int64_t H, int64_t W, int64_t D,
+                          const int32_t window_size[3], const int32_t shift_size[3], void* stream);
+
+/*
+ * Shifted-window region ids of every window token, (nW, N) uint8 written to HOST memory.
+ * Tokens i, j of a window attend to each other unmasked iff their ids are equal; otherwise the
+ * logit gets the upstream -100 (compute_3d_shifted_window_mask, swin3d.py:526-599, with the
+ * left/right merge of :502-514 when warped != 0 and pad tokens in their own group :589-591).
+ */
+int fa_shifted_window_groups(int64_t C, int64_t H, int64_t W, const int32_t window_size[3],
+                             const int32_t shift_size[3], int warped, uint8_t* groups_out);
+
+/*
+ * Window attention: out = softmax(q k^T * scale + bias) v per (window, head), N tokens.
+ * q, k, v, out are (Bwin, H, N, Dh) with element strides strides[0..11] =
+ * {q: window, head, token, k: ..., v: ..., out: ...}; head-dim stride 1.
+ * Mask (at most one): mask_u8 (nW, N, N) with 1 = masked, or group_ids (nW, N) with masked iff
+ * ids differ; window b uses mask index b % nW. A masked logit gets -100 added after scaling
+ * (upstream bias semantics, swin3d.py:597; CuTe kernel ops/cute/_kernel_bf16.py:361-365).
+ * Supported: Dh == 64, 1 <= N <= 144 for FA_ATTN_BF16 and FA_ATTN_FP32_3XTF32.
+ * Replaces window_attn_fwd_cute (ops/cute/window_attn_fwd.py:141-243).
+ */
+int fa_window_attention(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh,
+                        const void* q, const void* k, const void* v, void* out,
+                        const int64_t strides[12], const uint8_t* mask_u8,
+                        const uint8_t* group_ids, int64_t nW, float scale, void* stream);
+
+/*
+ * Same on the packed output of Linear(D, 3D): qkv (Bwin, N, 3, H, Dh) contiguous; out is
+ * (Bwin, H, N, Dh) for FA_LAYOUT_BHND or (Bwin, N, H*Dh) for FA_LAYOUT_BNC.
+ * Replaces window_attn_fwd_cute_qkvpacked (ops/cute/window_attn_fwd.py:246-353).
+ */
+int fa_window_attention_qkvpacked(int precision, int64_t Bwin, int64_t N, int64_t H, int64_t Dh,
+                                  const void* qkv, void* out, int out_layout,
+                                  const uint8_t* mask_u8, const uint8_t* group_ids, int64_t nW,
+                                  float scale, void* stream);
+
+/*
+ * Device status word of the attention kernels: 0 when every bounded wait of every launch since
+ * the last reset completed, else the code of the first wait that gave up. Synchronises the
+ * device. fa_attention_status_reset clears it (stream-ordered).
+ */
+int fa_attention_status(int* status_out);
+int fa_attention_status_reset(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASH_AURORA_B200_H */

@@ -1,0 +1,93 @@
+"""Host-side behaviour of the Python mirror that needs no GPU: upstream error types, module
+state-dict compatibility with the upstream backbone, workspace pool."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import flash_aurora_b200 as fa
+from flash_aurora_b200.swin3d import Swin3DTransformerBackbone, Swin3DTransformerBlock
+from _inputs import BACKBONE_SMALL, block_param_shapes
+
+
+def test_tf32_dtype_guard():
+    q, k, v = (torch.randn(2, 4, 16, 16) for _ in range(3))
+    with pytest.raises(AssertionError, match="float32"):
+        fa.window_attn_fwd_cute(q.bfloat16(), k.bfloat16(), v.bfloat16(), precision=fa.WinAttnPrecision.TF32_ACC_FP32)
+
+
+def test_bf16_mixed_dtype_guard():
+    q, k, v = (torch.randn(2, 4, 16, 16) for _ in range(3))
+    with pytest.raises(AssertionError, match="bfloat16"):
+        fa.window_attn_fwd_cute(q, k, v, precision=fa.WinAttnPrecision.BF16_MIXED)
+
+
+def test_dispatch_requires_cuda():
+    q, k, v = (torch.randn(2, 4, 16, 16) for _ in range(3))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fa.window_attn_dispatch(q, k, v)
+
+
+def test_layout_and_adaln_reject_cpu_tensors():
+    x = torch.randn(1, 4, 8, 16, 32)
+    with pytest.raises(ValueError, match="CUDA"):
+        fa.roll_pad_partition_windows_triton(x, (4, 8, 16), (2, 4, 4), (1, 2, 2))
+    with pytest.raises(ValueError, match="CUDA"):
+        fa.crop_roll_unmerge_windows_triton(torch.randn(16, 32, 32), (4, 8, 16), (2, 4, 4), (1, 2, 2))
+    with pytest.raises(ValueError, match="CUDA"):
+        fa.adaptive_layernorm_film_forward(torch.randn(1, 4, 8), torch.randn(1, 1, 8), torch.randn(1, 1, 8), 0.0)
+    with pytest.raises(ValueError, match="CUDA"):
+        fa.adaptive_layernorm_film_add_residual_forward(torch.randn(1, 4, 8), torch.randn(1, 4, 8),
+                                                        torch.randn(1, 1, 8), torch.randn(1, 1, 8), 0.0)
+
+
+def test_qkvpacked_argument_errors():
+    with pytest.raises(TypeError):
+        fa.window_attn_fwd_cute_qkvpacked(torch.zeros(2, 144, 384, dtype=torch.float16), 2)
+    with pytest.raises(ValueError, match="shape"):
+        fa.window_attn_fwd_cute_qkvpacked(torch.zeros(144, 384), 2)
+    with pytest.raises(ValueError, match="divisible"):
+        fa.window_attn_fwd_cute_qkvpacked(torch.zeros(2, 144, 380), 2)
+    with pytest.raises(ValueError, match="output_layout"):
+        fa.window_attn_fwd_cute_qkvpacked(torch.zeros(2, 144, 384), 2, output_layout="nhd")
+
+
+def test_block_state_dict_matches_upstream_keys():
+    blk = Swin3DTransformerBlock(dim=256, num_heads=4, time_dim=256, window_size=(2, 6, 12), shift_size=(1, 3, 6))
+    got = {k: tuple(v.shape) for k, v in blk.state_dict().items()}
+    assert got == block_param_shapes(256, 256)
+
+
+def test_backbone_state_dict_matches_upstream(golden):
+    d = golden("backbone_small.npz")
+    cfg = BACKBONE_SMALL
+    bb = Swin3DTransformerBackbone(embed_dim=cfg["embed_dim"], encoder_depths=cfg["encoder_depths"],
+                                   encoder_num_heads=cfg["encoder_num_heads"], decoder_depths=cfg["decoder_depths"],
+                                   decoder_num_heads=cfg["decoder_num_heads"], window_size=cfg["window"])
+    got = {k: str(tuple(v.shape)) for k, v in bb.state_dict().items()}
+    want = dict(zip([str(k) for k in d["keys"]], [str(s) for s in d["key_shapes"]]))
+    assert got == want
+
+
+def test_block_forward_refuses_cpu():
+    blk = Swin3DTransformerBlock(dim=64, num_heads=1, time_dim=64, window_size=(2, 6, 12))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        blk(torch.randn(1, 4 * 12 * 24, 64), torch.randn(1, 64), (4, 12, 24))
+
+
+def test_workspace_pool_reuses_buffers():
+    pool = fa.InferenceWorkspacePool()
+    a = pool.get("k", (2, 3), device="cpu", dtype=torch.float32)
+    b = pool.get("k", (2, 3), device="cpu", dtype=torch.float32)
+    c = pool.get("k", (2, 4), device="cpu", dtype=torch.float32)
+    assert a.data_ptr() == b.data_ptr() and c.shape == (2, 4)
+    pool.clear()
+
+
+def test_lead_time_expansion_matches_oracle():
+    from datetime import timedelta  # noqa: F401
+    from flash_aurora_b200.swin3d import lead_time_expansion
+    from oracle.block import lead_time_expansion as ref
+    h = torch.tensor([6.0, 0.5])
+    torch.testing.assert_close(lead_time_expansion(h, 512), ref(h, 512), rtol=0, atol=0)
