@@ -278,6 +278,96 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------------------------
+# Kernel-level workloads (BASELINE configs 2 and 3); not the driver's default line.
+# ----------------------------------------------------------------------------------------------
+def _time_launches(fn, iters, warmup=3, flush=None):
+    """Average device ms per call, CUDA events on the current stream, L2 flushed between calls."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(iters):
+        if flush is not None:
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        total += a.elapsed_time(b)
+    return total / iters
+
+
+def run_attention(args) -> None:
+    """Config 2: 1800 windows (grid (4,180,360), window (2,6,12)) x 8 heads x N=144 x d=64, packed
+    QKV, shifted-window region mask, bf16 and fp32 (3xTF32) I/O."""
+    import flash_aurora_b200 as fa
+    dev = torch.device("cuda", 0)
+    hbm, tflops_peak, kind = _peaks()
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    res, ws, ss = (4, 180, 360), (2, 6, 12), (1, 3, 6)
+    Bwin, H, N, Dh = 1800, 8, 144, 64
+    gids = fa.shifted_window_group_ids(res, ws, ss, device=dev)
+    flops = 4 * Bwin * H * N * N * Dh
+    for dtype, label in ((torch.bfloat16, "bf16"), (torch.float32, "fp32_3xtf32")):
+        qkv = (torch.randn(Bwin, N, 3 * H * Dh, device=dev, generator=g) / 8.0).to(dtype)
+        out = torch.empty(Bwin, N, H * Dh, device=dev, dtype=dtype)
+        for masked in (True, False):
+            fn = lambda: fa.window_attn_fwd_cute_qkvpacked(qkv, H, group_ids=gids if masked else None,
+                                                           output_layout="bnc", out=out)
+            ms = _time_launches(fn, args.steps, flush=flush)
+            nbytes = 4 * Bwin * H * N * Dh * qkv.element_size()
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            print(json.dumps({
+                "workload": f"config2 window attention {label} {'masked' if masked else 'unmasked'}",
+                "ms": round(ms, 4), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                "tensor_peak_tflops": tflops_peak, "tensor_frac": round(flops / (ms * 1e-3) / 1e12 / tflops_peak, 3),
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                             "frac": round(gbs / hbm, 3), "peak_kind": kind, "algorithmic_bytes": nbytes},
+            }), flush=True)
+
+
+def run_layout_adaln(args) -> None:
+    """Config 3: grid (4,45,90), D 2048, padded (4,48,96) -> 128 windows, shift (1,3,6)."""
+    import flash_aurora_b200 as fa
+    dev = torch.device("cuda", 0)
+    hbm, _, kind = _peaks()
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    res, ws, ss = (4, 45, 90), (2, 6, 12), (1, 3, 6)
+    C, H, W = res
+    D = 2048
+    L = C * H * W
+    x = torch.randn(1, C, H, W, D, device=dev, generator=g)
+    win = fa.roll_pad_partition_windows(x, res, ws, ss)
+    branch = torch.randn(1, L, D, device=dev, generator=g).bfloat16()
+    resid = torch.randn(1, L, D, device=dev, generator=g)
+    scale = torch.randn(1, 1, D, device=dev, generator=g) * 0.1
+    shift = torch.randn(1, 1, D, device=dev, generator=g) * 0.1
+    nwin = win.shape[0] * win.shape[1]
+    cases = [
+        ("partition fp32->fp32", lambda: fa.roll_pad_partition_windows(x, res, ws, ss), L * D * 4 + nwin * D * 4),
+        ("partition fp32->bf16", lambda: fa.roll_pad_partition_windows(x, res, ws, ss, out_dtype=torch.bfloat16),
+         L * D * 4 + nwin * D * 2),
+        ("unmerge fp32->fp32", lambda: fa.crop_roll_unmerge_windows(win, res, ws, ss), 2 * L * D * 4),
+        ("adaln+residual bf16 x, fp32 residual -> fp32",
+         lambda: fa.adaptive_layernorm_film_add_residual_forward(resid, branch, scale, shift, 0.0, output_fp32=True),
+         L * D * (2 + 4 + 4)),
+        ("unmerge+adaln+residual fp32 windows -> fp32",
+         lambda: fa.unmerge_adaptive_layernorm_film_add_residual(win, resid, scale, shift, res, ws, ss),
+         L * D * (4 + 4 + 4)),
+    ]
+    for name, fn, nbytes in cases:
+        ms = _time_launches(fn, args.steps, flush=flush)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"workload": f"config3 {name}", "ms": round(ms, 4),
+                          "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                       "frac": round(gbs / hbm, 3), "peak_kind": kind, "algorithmic_bytes": nbytes}}),
+              flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -285,9 +375,14 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["backbone", "attention", "layout_adaln"], default="backbone")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "attention":
+        return run_attention(args)
+    if args.workload == "layout_adaln":
+        return run_layout_adaln(args)
     if args.impl == "reference":
         run_reference(args)
     else:

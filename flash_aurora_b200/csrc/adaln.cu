@@ -163,7 +163,8 @@ int launch_adaln(const AdaArgs& a, bool vec, cudaStream_t s) {
 
 int run_adaln(AdaArgs a, int x_dtype, int residual_dtype, int mod_dtype, int out_dtype,
               cudaStream_t s) {
-  FA_REQUIRE(a.x && a.scale && a.shift && a.out, FA_ERR_INVALID, "null tensor pointer");
+  FA_REQUIRE((a.x && a.scale && a.shift && a.out) || a.B * a.L == 0 || a.D == 0, FA_ERR_INVALID,
+             "null tensor pointer");
   FA_REQUIRE(x_dtype == FA_F32 || x_dtype == FA_BF16, FA_ERR_INVALID, "x dtype must be FA_F32 or FA_BF16");
   FA_REQUIRE(out_dtype == FA_F32 || out_dtype == FA_BF16, FA_ERR_INVALID, "out dtype must be FA_F32 or FA_BF16");
   FA_REQUIRE(mod_dtype == FA_F32 || mod_dtype == FA_BF16, FA_ERR_INVALID, "scale/shift dtype must be FA_F32 or FA_BF16");

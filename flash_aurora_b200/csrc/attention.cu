@@ -435,14 +435,16 @@ int run(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const voi
         const uint8_t* group_ids, int64_t nW, float scale, void* stream) {
   FA_REQUIRE(precision == FA_ATTN_BF16 || precision == FA_ATTN_FP32_3XTF32, FA_ERR_INVALID,
              "precision must be FA_ATTN_BF16 or FA_ATTN_FP32_3XTF32");
-  FA_REQUIRE(q && k && v && out && strides, FA_ERR_INVALID, "null tensor pointer");
+  FA_REQUIRE(strides, FA_ERR_INVALID, "null stride pointer");
   FA_REQUIRE(Bwin >= 0 && H >= 1 && N >= 1, FA_ERR_INVALID, "invalid attention shape");
+  FA_REQUIRE((q && k && v && out) || Bwin == 0, FA_ERR_INVALID, "null tensor pointer");
   FA_REQUIRE(Dh == 64, FA_ERR_UNSUPPORTED, "window attention supports head_dim 64");
   FA_REQUIRE(N <= kMaxN, FA_ERR_UNSUPPORTED, "window attention supports N <= 144 tokens");
   FA_REQUIRE(!(mask_u8 && group_ids), FA_ERR_INVALID, "pass at most one of mask_u8 / group_ids");
   FA_REQUIRE(!(mask_u8 || group_ids) || nW >= 1, FA_ERR_INVALID, "nW must be >= 1 with a mask");
   FA_REQUIRE(Bwin * H < ((int64_t)1 << 31), FA_ERR_INVALID, "too many (window, head) tiles");
   if (Bwin == 0) return FA_OK;
+  FA_REQUIRE(q && k && v && out, FA_ERR_INVALID, "null tensor pointer");
   const bool f32 = precision == FA_ATTN_FP32_3XTF32;
   const int64_t es = f32 ? 4 : 2;
   const void* ptrs[3] = {q, k, v};
@@ -496,7 +498,7 @@ extern "C" int fa_window_attention_qkvpacked(int precision, int64_t Bwin, int64_
                                              int64_t Dh, const void* qkv, void* out, int out_layout,
                                              const uint8_t* mask_u8, const uint8_t* group_ids,
                                              int64_t nW, float scale, void* stream) {
-  FA_REQUIRE(qkv && out, FA_ERR_INVALID, "null tensor pointer");
+  FA_REQUIRE((qkv && out) || Bwin == 0, FA_ERR_INVALID, "null tensor pointer");
   FA_REQUIRE(out_layout == FA_LAYOUT_BHND || out_layout == FA_LAYOUT_BNC, FA_ERR_INVALID,
              "out_layout must be FA_LAYOUT_BHND or FA_LAYOUT_BNC");
   FA_REQUIRE(precision == FA_ATTN_BF16 || precision == FA_ATTN_FP32_3XTF32, FA_ERR_INVALID,

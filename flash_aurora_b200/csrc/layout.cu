@@ -114,13 +114,14 @@ int launch_unmerge(const void* w, void* out, const LayoutParams& p, int64_t B, i
 int check_layout_args(const void* a, int adt, const void* b, int bdt, int64_t B, int64_t C,
                       int64_t H, int64_t W, int64_t D, const int32_t* ws, const int32_t* ss,
                       Geometry* g) {
-  FA_REQUIRE(a && b, FA_ERR_INVALID, "null tensor pointer");
   FA_REQUIRE(adt == FA_F32 || adt == FA_BF16, FA_ERR_INVALID, "dtype must be FA_F32 or FA_BF16");
   FA_REQUIRE(bdt == FA_F32 || bdt == FA_BF16, FA_ERR_INVALID, "dtype must be FA_F32 or FA_BF16");
   FA_REQUIRE(B >= 0 && D >= 0, FA_ERR_INVALID, "negative size");
   FA_REQUIRE(D <= (1 << 20), FA_ERR_INVALID, "D too large");
   int rc = make_geometry(C, H, W, ws, ss, g);
   if (rc != FA_OK) return rc;
+  // Empty tensors may carry null pointers; only non-empty ones must be valid.
+  FA_REQUIRE((a && b) || B == 0 || D == 0, FA_ERR_INVALID, "null tensor pointer");
   FA_REQUIRE(B * g->nW * g->N < (int64_t)1 << 40, FA_ERR_INVALID, "tensor too large");
   return FA_OK;
 }
