@@ -16,7 +16,9 @@
 // scale, window index b % nW) and the CuTe kernel (ops/cute/_kernel_bf16.py:361-365).
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "attention.cuh"
 #include "fa_common.cuh"
@@ -377,6 +379,317 @@ attn_sync_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
 }
 
 // ------------------------------------------------------------------------------------------
+// BF16 kernel on the 5th-generation tensor cores (tcgen05 / UMMA, accumulators in TMEM).
+//
+// Warp roles (256 threads, one CTA per SM, persistent over (window, head) tiles):
+//   warp 0      TMA producer: Q, K, V of a tile into a 3-stage ring (128-byte swizzle).
+//   warp 1      owns TMEM (512 columns) and, from one thread, issues the UMMAs:
+//                 S[b] = Q[0:128] K^T   (M=128, N=144, K=64; 4 x K16, A and B K-major)
+//                 O[b] = P V            (M=128, N=64,  K=144; 9 x K16, P K-major, V MN-major)
+//               completion is signalled with tcgen05.commit on mbarriers.
+//   warp 2      query rows 128..143 on warp-level mma.sync (an M=128 UMMA for 16 rows would
+//               double the TMEM and softmax work of the tile).
+//   warps 4..7  softmax + epilogue of rows 0..127, one TMEM lane (row) per thread: S row from
+//               TMEM, scale + mask + exp2 + row sum in fp32, P row to shared memory as bf16 in the
+//               UMMA A-operand layout, then O row from TMEM scaled by 1/sum -> bf16 -> global.
+// S and O are double-buffered in TMEM so the S UMMA of tile i+1 and the PV UMMA of tile i overlap
+// the softmax of the neighbouring tile. Every wait is bounded (status word + abort flag).
+// ------------------------------------------------------------------------------------------
+namespace tc {
+
+constexpr int kStages = 3;
+constexpr int kStageBytes = 3 * kTileBytes;  // Q, K, V (bf16, 144 x 128 B each)
+constexpr int kPChunk = 128 * 128;          // 64 keys x 128 rows of bf16
+constexpr int kPBytes = 3 * kPChunk;        // keys 0-63, 64-127, 128-143 (+ unused tail)
+constexpr int kThreads = 256;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS0 = 0, kColS1 = 160, kColO0 = 320, kColO1 = 384;
+constexpr int kNumBars = 17;
+constexpr int kSmem = kStages * kStageBytes + kPBytes + kNumBars * 8 + 16 + 1024;
+constexpr uint32_t kIdescS = ptx::make_idesc(1, 128, kMaxN, false, false);
+constexpr uint32_t kIdescO = ptx::make_idesc(1, 128, 64, false, true);
+
+// Barrier slots.
+enum { kFull = 0, kEmpty = 3, kSFull = 6, kSFree = 8, kPFull = 10, kPEmpty = 11, kOFull = 12, kOFree = 14,
+       kDone = 16 };
+
+// Masked-logit bias of the 144 keys of one row, as a bit per key (bit j set = masked).
+template <int kMask>
+__device__ __forceinline__ void row_mask_bits(const Params& p, int mw, int row, uint32_t bits[5]) {
+#pragma unroll
+  for (int i = 0; i < 5; ++i) bits[i] = 0u;
+  if constexpr (kMask == kGroups) {
+    const uint8_t* g = p.mask + (int64_t)mw * p.N;
+    const uint32_t rep = (row < p.N ? (uint32_t)__ldg(g + row) : 0u) * 0x01010101u;
+    for (int j4 = 0; j4 < (p.N + 3) / 4; ++j4) {
+      uint32_t w = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int key = 4 * j4 + b;
+        w |= (key < p.N ? (uint32_t)__ldg(g + key) : 0u) << (8 * b);
+      }
+      const uint32_t ne = __vcmpne4(w, rep);  // 0xff per differing byte
+      const uint32_t nib = (ne & 1u) | ((ne >> 7) & 2u) | ((ne >> 14) & 4u) | ((ne >> 21) & 8u);
+      bits[j4 >> 3] |= nib << ((j4 & 7) * 4);
+    }
+  } else if constexpr (kMask == kMaskU8) {
+    if (row < p.N) {
+      const uint8_t* m = p.mask + ((int64_t)mw * p.N + row) * p.N;
+      for (int key = 0; key < p.N; ++key)
+        if (__ldg(m + key)) bits[key >> 5] |= 1u << (key & 31);
+    }
+  }
+}
+
+template <int kMask>
+__global__ void __launch_bounds__(kThreads, 1)
+attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                    const __grid_constant__ CUtensorMap tmv, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t sP = sbase + kStages * kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kPBytes);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  const uint32_t bar0 = smem_u32(bars);
+  auto BAR = [&](int slot) -> uint32_t { return bar0 + 8u * (uint32_t)slot; };
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(BAR(kFull + s), 1);
+      mbar_init(BAR(kEmpty + s), 2);  // UMMA commit + remainder warp
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(BAR(kSFull + b), 1);
+      mbar_init(BAR(kSFree + b), 4);
+      mbar_init(BAR(kOFull + b), 1);
+      mbar_init(BAR(kOFree + b), 4);
+    }
+    mbar_init(BAR(kPFull), 4);
+    mbar_init(BAR(kPEmpty), 1);
+    mbar_init(BAR(kDone), 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  volatile int* abort = &abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmq);
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      int last_par[kStages] = {-1, -1, -1};
+      int i = 0;
+      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
+        const int s = i % kStages;
+        const uint32_t ph = (uint32_t)((i / kStages) & 1);
+        if (!mbar_wait(BAR(kEmpty + s), ph ^ 1u, abort, p.status, 11, kTimeoutNs)) break;
+        const int w = t / p.H, h = t - w * p.H;
+        const uint32_t dst = sbase + s * kStageBytes;
+        mbar_arrive_expect_tx(BAR(kFull + s), kStageBytes);
+        tma_load_4d(dst, &tmq, BAR(kFull + s), 0, 0, h, w);
+        tma_load_4d(dst + kTileBytes, &tmk, BAR(kFull + s), 0, 0, h, w);
+        tma_load_4d(dst + 2 * kTileBytes, &tmv, BAR(kFull + s), 0, 0, h, w);
+        last_par[s] = (int)ph;
+      }
+      int no_abort = 0;
+      for (int s = 0; s < kStages; ++s)
+        if (last_par[s] >= 0) mbar_wait(BAR(kFull + s), (uint32_t)last_par[s], &no_abort, p.status, 12, kTimeoutNs);
+    }
+  } else if (warp == 1) {
+    // ---------------- UMMA issuer ----------------
+    if (lane == 0) {
+      auto issue_pv = [&](int j) -> bool {
+        const int s = j % kStages, ob = j & 1;
+        if (!mbar_wait(BAR(kPFull), (uint32_t)(j & 1), abort, p.status, 13, kTimeoutNs)) return false;
+        if (!mbar_wait(BAR(kOFree + ob), (uint32_t)(((j >> 1) & 1) ^ 1), abort, p.status, 14, kTimeoutNs))
+          return false;
+        tc_fence_after();
+        const uint32_t sV = sbase + s * kStageBytes + 2 * kTileBytes;
+        const uint32_t dO = tmem + (ob ? kColO1 : kColO0);
+#pragma unroll
+        for (int k = 0; k < 9; ++k) {
+          const uint64_t a = desc_sw128(sP + (k >> 2) * kPChunk + (k & 3) * 32, 16, 1024);
+          const uint64_t b = desc_sw128(sV + k * 2048, kTileBytes, 1024);
+          umma_f16(dO, a, b, kIdescO, k > 0 ? 1u : 0u);
+        }
+        umma_commit(BAR(kOFull + ob));
+        umma_commit(BAR(kPEmpty));
+        umma_commit(BAR(kEmpty + s));
+        return true;
+      };
+      int i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
+        const int s = i % kStages, sb = i & 1;
+        if (!mbar_wait(BAR(kFull + s), (uint32_t)((i / kStages) & 1), abort, p.status, 15, kTimeoutNs)) { ok = false; break; }
+        if (!mbar_wait(BAR(kSFree + sb), (uint32_t)(((i >> 1) & 1) ^ 1), abort, p.status, 16, kTimeoutNs)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sQ = sbase + s * kStageBytes, sK = sQ + kTileBytes;
+        const uint32_t dS = tmem + (sb ? kColS1 : kColS0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_f16(dS, desc_sw128(sQ + k * 32, 16, 1024), desc_sw128(sK + k * 32, 16, 1024), kIdescS, k > 0 ? 1u : 0u);
+        umma_commit(BAR(kSFull + sb));
+        if (i > 0 && !issue_pv(i - 1)) { ok = false; break; }
+      }
+      if (ok && i > 0) issue_pv(i - 1);
+      umma_commit(BAR(kDone));
+      int no_abort = 0;
+      mbar_wait(BAR(kDone), 0, &no_abort, p.status, 17, kTimeoutNs);
+    }
+  } else if (warp == 2) {
+    // ---------------- rows 128..143 on mma.sync ----------------
+    int i = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
+      const int s = i % kStages;
+      if (!mbar_wait(BAR(kFull + s), (uint32_t)((i / kStages) & 1), abort, p.status, 18, kTimeoutNs)) break;
+      if (p.N > 128) {
+        const int w = t / p.H, h = t - w * p.H;
+        MaskView<kMask> mv;
+        mv.N = p.N;
+        const int mw = w % p.nW;
+        if constexpr (kMask == kGroups) mv.base = p.mask + (int64_t)mw * p.N;
+        else if constexpr (kMask == kMaskU8) mv.base = p.mask + (int64_t)mw * p.N * p.N;
+        else mv.base = nullptr;
+        const uint32_t st = sbase + s * kStageBytes;
+        rows16_bf16<kMask>(st, st + kTileBytes, st + 2 * kTileBytes, 128, p.N, p.scale_log2, mv,
+                           reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)w * p.os_w + (int64_t)h * p.os_h,
+                           p.os_n, lane);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kEmpty + s));
+    }
+  } else if (warp >= 4) {
+    // ---------------- softmax + epilogue, rows 0..127 ----------------
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    float l_prev = 1.f;
+    int t_prev = -1, j_prev = -1;
+
+    auto epilogue = [&](int j, int t, float l) -> bool {
+      const int ob = j & 1;
+      if (!mbar_wait(BAR(kOFull + ob), (uint32_t)((j >> 1) & 1), abort, p.status, 19, kTimeoutNs)) return false;
+      tc_fence_after();
+      uint32_t o[4][16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld16(tmem + lane_addr + (ob ? kColO1 : kColO0) + 16 * c, o[c]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kOFree + ob));
+      if (row < p.N) {
+        const int w = t / p.H, h = t - w * p.H;
+        const float inv = 1.f / l;
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)w * p.os_w +
+                                              (int64_t)h * p.os_h + (int64_t)row * p.os_n);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint4 a, b;
+          a.x = pack_bf16x2(__uint_as_float(o[c][0]) * inv, __uint_as_float(o[c][1]) * inv);
+          a.y = pack_bf16x2(__uint_as_float(o[c][2]) * inv, __uint_as_float(o[c][3]) * inv);
+          a.z = pack_bf16x2(__uint_as_float(o[c][4]) * inv, __uint_as_float(o[c][5]) * inv);
+          a.w = pack_bf16x2(__uint_as_float(o[c][6]) * inv, __uint_as_float(o[c][7]) * inv);
+          b.x = pack_bf16x2(__uint_as_float(o[c][8]) * inv, __uint_as_float(o[c][9]) * inv);
+          b.y = pack_bf16x2(__uint_as_float(o[c][10]) * inv, __uint_as_float(o[c][11]) * inv);
+          b.z = pack_bf16x2(__uint_as_float(o[c][12]) * inv, __uint_as_float(o[c][13]) * inv);
+          b.w = pack_bf16x2(__uint_as_float(o[c][14]) * inv, __uint_as_float(o[c][15]) * inv);
+          dst[2 * c] = a;
+          dst[2 * c + 1] = b;
+        }
+      }
+      return true;
+    };
+
+    int i = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
+      const int sb = i & 1;
+      const int w = t / p.H;
+      uint32_t mbits[5];
+      row_mask_bits<kMask>(p, w % p.nW, row, mbits);
+      if (!mbar_wait(BAR(kSFull + sb), (uint32_t)((i >> 1) & 1), abort, p.status, 20, kTimeoutNs)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sr[9][16];
+#pragma unroll
+      for (int c = 0; c < 9; ++c) tmem_ld16(tmem + lane_addr + (sb ? kColS1 : kColS0) + 16 * c, sr[c]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kSFree + sb));
+      // logits -> log2 domain, mask, row max
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 9; ++c) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int key = 16 * c + e;
+          float y = __uint_as_float(sr[c][e]) * p.scale_log2;
+          if constexpr (kMask != kNoMask) {
+            if ((mbits[key >> 5] >> (key & 31)) & 1u) y += kMaskedLog2;
+          }
+          if (key >= p.N) y = -INFINITY;
+          sr[c][e] = __float_as_uint(y);
+          mx = fmaxf(mx, y);
+        }
+      }
+      float l = 0.f;
+      uint32_t pk[9][8];
+#pragma unroll
+      for (int c = 0; c < 9; ++c) {
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+          const float a = ex2(__uint_as_float(sr[c][e]) - mx);
+          const float b = ex2(__uint_as_float(sr[c][e + 1]) - mx);
+          l += a + b;
+          pk[c][e >> 1] = pack_bf16x2(a, b);
+        }
+      }
+      // P row -> shared memory (UMMA A operand, K-major, 128-byte swizzle, 64-key chunks).
+      if (!mbar_wait(BAR(kPEmpty), (uint32_t)((i & 1) ^ 1), abort, p.status, 21, kTimeoutNs)) { ok = false; break; }
+#pragma unroll
+      for (int c = 0; c < 9; ++c) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int j16 = 2 * c + hh;            // 8-key group 0..17
+          const int chunk = j16 >> 3, jj = j16 & 7;
+          const uint32_t addr = sP + chunk * kPChunk + row * 128 + ((jj ^ (row & 7)) << 4);
+          st_shared_v4(addr, pk[c][4 * hh], pk[c][4 * hh + 1], pk[c][4 * hh + 2], pk[c][4 * hh + 3]);
+        }
+      }
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kPFull));
+      if (j_prev >= 0 && !epilogue(j_prev, t_prev, l_prev)) { ok = false; break; }
+      j_prev = i;
+      t_prev = t;
+      l_prev = l;
+    }
+    if (ok && j_prev >= 0) epilogue(j_prev, t_prev, l_prev);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------------------------------------
 // Host side
 // ------------------------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
@@ -411,6 +724,16 @@ int make_map(CUtensorMap* map, const void* base, bool f32, int64_t Bwin, int64_t
   return FA_OK;
 }
 
+template <int kMask>
+int launch_tc_bf16(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p,
+                   cudaStream_t s) {
+  auto kern = tc::attn_tc_bf16_kernel<kMask>;
+  FA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmem));
+  const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
+  kern<<<grid, tc::kThreads, tc::kSmem, s>>>(mq, mk, mv, p);
+  return check_launch("attn_tc_bf16_kernel");
+}
+
 template <bool kF32, int kMask>
 int launch_sync(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p,
                 cudaStream_t s) {
@@ -420,6 +743,13 @@ int launch_sync(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
   kern<<<grid, kThreads, C::kSmem, s>>>(mq, mk, mv, p);
   return check_launch("attn_sync_kernel");
+}
+
+// FA_ATTN_BF16_KERNEL=mma_sync selects the warp-level kernel for bf16 (kept as a cross-check of
+// the tensor-memory kernel); the default is the tcgen05 kernel.
+bool use_sync_bf16() {
+  const char* e = getenv("FA_ATTN_BF16_KERNEL");
+  return e && std::string(e) == "mma_sync";
 }
 
 }  // namespace
@@ -477,9 +807,16 @@ int run(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const voi
     if (kind == kMaskU8) return launch_sync<true, kMaskU8>(mq, mk, mv, p, s);
     return launch_sync<true, kNoMask>(mq, mk, mv, p, s);
   }
-  if (kind == kGroups) return launch_sync<false, kGroups>(mq, mk, mv, p, s);
-  if (kind == kMaskU8) return launch_sync<false, kMaskU8>(mq, mk, mv, p, s);
-  return launch_sync<false, kNoMask>(mq, mk, mv, p, s);
+  // The tensor-memory kernel stores 16-byte output rows: needs 16-byte aligned rows.
+  const bool out16 = aligned16(out) && p.os_w % 8 == 0 && p.os_h % 8 == 0 && p.os_n % 8 == 0;
+  if (use_sync_bf16() || !out16) {
+    if (kind == kGroups) return launch_sync<false, kGroups>(mq, mk, mv, p, s);
+    if (kind == kMaskU8) return launch_sync<false, kMaskU8>(mq, mk, mv, p, s);
+    return launch_sync<false, kNoMask>(mq, mk, mv, p, s);
+  }
+  if (kind == kGroups) return launch_tc_bf16<kGroups>(mq, mk, mv, p, s);
+  if (kind == kMaskU8) return launch_tc_bf16<kMaskU8>(mq, mk, mv, p, s);
+  return launch_tc_bf16<kNoMask>(mq, mk, mv, p, s);
 }
 
 }  // namespace attn

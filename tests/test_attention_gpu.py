@@ -160,3 +160,21 @@ def test_status_word_clean_after_launches():
     st = ctypes.c_int(-1)
     _lib.check(_lib.load().fa_attention_status(ctypes.byref(st)), "status")
     assert st.value == 0
+
+
+@pytest.mark.parametrize("has_mask", [False, True])
+@pytest.mark.parametrize("N", [144, 96, 130])
+def test_tensor_memory_kernel_matches_warp_mma_kernel(monkeypatch, has_mask, N):
+    # The bf16 default is the tcgen05 kernel; FA_ATTN_BF16_KERNEL=mma_sync selects the warp-level
+    # kernel. Both must agree to bf16 rounding on the same inputs.
+    Bwin, H = 12, 4
+    q, k, v = (t.bfloat16().cuda() for t in _qkv(Bwin, H, N, 64, seed=9, scale=1.0))
+    bias = _half_bias(3, N).cuda() if has_mask else None
+    a = fa.window_attn_fwd_cute(q, k, v, bias)
+    monkeypatch.setenv("FA_ATTN_BF16_KERNEL", "mma_sync")
+    b = fa.window_attn_fwd_cute(q, k, v, bias)
+    monkeypatch.delenv("FA_ATTN_BF16_KERNEL")
+    ref = OB.window_attention_core(q.double().cpu(), k.double().cpu(), v.double().cpu(),
+                                   bias.double().cpu() if bias is not None else None)
+    assert _rel_l2(a, ref) <= 1e-2 and _rel_l2(b, ref) <= 1e-2
+    assert (a.float() - b.float()).abs().max().item() <= 2e-2
