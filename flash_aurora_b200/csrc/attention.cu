@@ -55,6 +55,18 @@ struct MaskView {
     else if constexpr (kMask == kMaskU8) return (int)rtag < N && __ldg(base + (int64_t)rtag * N + key) != 0;
     else return false;
   }
+  // Key-side data of keys (key, key + 1) for two rows, one load per row pair when aligned.
+  __device__ __forceinline__ uint32_t key_pair(int key) const {
+    if constexpr (kMask == kGroups) {
+      if (key + 1 < N && ((reinterpret_cast<uintptr_t>(base) + key) & 1) == 0)
+        return __ldg(reinterpret_cast<const unsigned short*>(base + key));
+      const uint32_t lo = key < N ? __ldg(base + key) : 0u;
+      const uint32_t hi = key + 1 < N ? __ldg(base + key + 1) : 0u;
+      return lo | (hi << 8);
+    } else {
+      return 0u;
+    }
+  }
 };
 
 // ------------------------------------------------------------------------------------------
@@ -88,6 +100,7 @@ __device__ __forceinline__ void rows16_bf16(uint32_t sQ, uint32_t sK, uint32_t s
   float mxa = -INFINITY, mxb = -INFINITY;
 #pragma unroll
   for (int j = 0; j < 18; ++j) {
+    const uint32_t kp = mv.key_pair(8 * j + 2 * q);
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int key = 8 * j + 2 * q + e;
@@ -95,7 +108,11 @@ __device__ __forceinline__ void rows16_bf16(uint32_t sQ, uint32_t sK, uint32_t s
       if (key >= N) {
         xa = -INFINITY;
         xb = -INFINITY;
-      } else if constexpr (kMask != kNoMask) {
+      } else if constexpr (kMask == kGroups) {
+        const uint32_t kg = (kp >> (8 * e)) & 0xffu;
+        if (kg != ta) xa += kMaskedLog2;
+        if (kg != tb) xb += kMaskedLog2;
+      } else if constexpr (kMask == kMaskU8) {
         if (mv.masked(ta, key)) xa += kMaskedLog2;
         if (mv.masked(tb, key)) xb += kMaskedLog2;
       }
@@ -201,6 +218,7 @@ __device__ __forceinline__ void rows16_tf32x3(uint32_t sQ, uint32_t sK, uint32_t
   float mxa = -INFINITY, mxb = -INFINITY;
 #pragma unroll
   for (int j = 0; j < 18; ++j) {
+    const uint32_t kp = mv.key_pair(8 * j + 2 * q);
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int key = 8 * j + 2 * q + e;
@@ -208,7 +226,11 @@ __device__ __forceinline__ void rows16_tf32x3(uint32_t sQ, uint32_t sK, uint32_t
       if (key >= N) {
         xa = -INFINITY;
         xb = -INFINITY;
-      } else if constexpr (kMask != kNoMask) {
+      } else if constexpr (kMask == kGroups) {
+        const uint32_t kg = (kp >> (8 * e)) & 0xffu;
+        if (kg != ta) xa += kMaskedLog2;
+        if (kg != tb) xb += kMaskedLog2;
+      } else if constexpr (kMask == kMaskU8) {
         if (mv.masked(ta, key)) xa += kMaskedLog2;
         if (mv.masked(tb, key)) xb += kMaskedLog2;
       }
@@ -413,30 +435,46 @@ constexpr uint32_t kIdescO = ptx::make_idesc(1, 128, 64, false, true);
 enum { kFull = 0, kEmpty = 3, kSFull = 6, kSFree = 8, kPFull = 10, kPEmpty = 11, kOFull = 12, kOFree = 14,
        kDone = 16 };
 
-// Masked-logit bias of the 144 keys of one row, as a bit per key (bit j set = masked).
+// Masked keys of one row as a bit per key (bit j set = masked). Reads the window's region ids
+// (or the row of the u8 mask) 16 bytes at a time when N is a multiple of 16.
+__device__ __forceinline__ uint32_t nibble_of_bytes(uint32_t ne) {
+  // ne: 0xff per byte that marks a masked key -> 4 bits
+  return (ne & 1u) | ((ne >> 7) & 2u) | ((ne >> 14) & 4u) | ((ne >> 21) & 8u);
+}
+
 template <int kMask>
 __device__ __forceinline__ void row_mask_bits(const Params& p, int mw, int row, uint32_t bits[5]) {
 #pragma unroll
   for (int i = 0; i < 5; ++i) bits[i] = 0u;
-  if constexpr (kMask == kGroups) {
-    const uint8_t* g = p.mask + (int64_t)mw * p.N;
-    const uint32_t rep = (row < p.N ? (uint32_t)__ldg(g + row) : 0u) * 0x01010101u;
-    for (int j4 = 0; j4 < (p.N + 3) / 4; ++j4) {
-      uint32_t w = 0;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const int key = 4 * j4 + b;
-        w |= (key < p.N ? (uint32_t)__ldg(g + key) : 0u) << (8 * b);
-      }
-      const uint32_t ne = __vcmpne4(w, rep);  // 0xff per differing byte
-      const uint32_t nib = (ne & 1u) | ((ne >> 7) & 2u) | ((ne >> 14) & 4u) | ((ne >> 21) & 8u);
-      bits[j4 >> 3] |= nib << ((j4 & 7) * 4);
+  if constexpr (kMask == kNoMask) {
+    return;
+  } else {
+    const uint8_t* src;
+    uint32_t ref = 0;
+    if constexpr (kMask == kGroups) {
+      src = p.mask + (int64_t)mw * p.N;
+      ref = (row < p.N ? (uint32_t)__ldg(src + row) : 0u) * 0x01010101u;
+    } else {
+      if (row >= p.N) return;
+      src = p.mask + ((int64_t)mw * p.N + row) * p.N;
     }
-  } else if constexpr (kMask == kMaskU8) {
-    if (row < p.N) {
-      const uint8_t* m = p.mask + ((int64_t)mw * p.N + row) * p.N;
-      for (int key = 0; key < p.N; ++key)
-        if (__ldg(m + key)) bits[key >> 5] |= 1u << (key & 31);
+    if ((p.N & 15) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+      for (int v = 0; v < p.N / 16; ++v) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(src) + v);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t ne = __vcmpne4(ws[k], ref);
+          const int j4 = 4 * v + k;  // word index: keys 4*j4 .. 4*j4+3
+          bits[j4 >> 3] |= nibble_of_bytes(ne) << ((j4 & 7) * 4);
+        }
+      }
+    } else {
+      for (int key = 0; key < p.N; ++key) {
+        const uint32_t b = __ldg(src + key);
+        const bool m = (kMask == kGroups) ? (b != (ref & 0xffu)) : (b != 0u);
+        if (m) bits[key >> 5] |= 1u << (key & 31);
+      }
     }
   }
 }
@@ -718,7 +756,7 @@ int make_map(CUtensorMap* map, const void* base, bool f32, int64_t Bwin, int64_t
   cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
                         const_cast<void*>(base), dims, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   FA_REQUIRE(r == CUDA_SUCCESS, FA_ERR_CUDA, "cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) + ")");
   return FA_OK;
