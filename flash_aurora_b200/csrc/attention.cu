@@ -403,42 +403,44 @@ attn_sync_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
 // ------------------------------------------------------------------------------------------
 // BF16 kernel on the 5th-generation tensor cores (tcgen05 / UMMA, accumulators in TMEM).
 //
+// A window has 144 query rows; an M=128 UMMA covers 128. Every tile therefore runs two
+// query blocks through the tensor cores: rows 0..127 and rows 16..143 (the second block reuses
+// the same shared-memory tiles at a 16-row offset; only its last 16 rows, 128..143, are kept).
+//
 // Warp roles (256 threads, one CTA per SM, persistent over (window, head) tiles):
 //   warp 0      TMA producer: Q, K, V of a tile into a 3-stage ring (128-byte swizzle).
 //   warp 1      owns TMEM (512 columns) and, from one thread, issues the UMMAs:
-//                 S[b] = Q[0:128] K^T   (M=128, N=144, K=64; 4 x K16, A and B K-major)
-//                 O[b] = P V            (M=128, N=64,  K=144; 9 x K16, P K-major, V MN-major)
-//               completion is signalled with tcgen05.commit on mbarriers.
-//   warp 2      query rows 128..143 on warp-level mma.sync (an M=128 UMMA for 16 rows would
-//               double the TMEM and softmax work of the tile).
-//   warps 4..7  softmax + epilogue of rows 0..127, one TMEM lane (row) per thread: S row from
-//               TMEM, scale + mask + exp2 + row sum in fp32, P row to shared memory as bf16 in the
-//               UMMA A-operand layout, then O row from TMEM scaled by 1/sum -> bf16 -> global.
-// S and O are double-buffered in TMEM so the S UMMA of tile i+1 and the PV UMMA of tile i overlap
-// the softmax of the neighbouring tile. Every wait is bounded (status word + abort flag).
+//                 S  = Q[0:128]  K^T, S2 = Q[16:144] K^T   (M=128, N=144, K=64, K-major A and B)
+//                 O  = P[0:128]  V,   O2 = P[16:144] V     (M=128, N=64, K=144, V MN-major)
+//               and signals completion with tcgen05.commit on mbarriers.
+//   warps 4..7  softmax + epilogue of rows 0..127: one TMEM lane (row) per thread; S row from TMEM,
+//               scale + mask + exp2 + row sum in fp32, P row (bf16) into shared memory in the UMMA
+//               A-operand layout; then O row from TMEM, times 1/sum, bf16, to global memory.
+//   warp 3      the same for rows 128..143, read from S2/O2 lanes 112..127 (its TMEM quadrant).
+// S is read into registers at the start of the softmax and released at once, so the S UMMAs of
+// tile i+1 run under the softmax of tile i; O is double-buffered. Every wait is bounded.
 // ------------------------------------------------------------------------------------------
 namespace tc {
 
 constexpr int kStages = 3;
 constexpr int kStageBytes = 3 * kTileBytes;  // Q, K, V (bf16, 144 x 128 B each)
-constexpr int kPChunk = 128 * 128;          // 64 keys x 128 rows of bf16
-constexpr int kPBytes = 3 * kPChunk;        // keys 0-63, 64-127, 128-143 (+ unused tail)
+constexpr int kPChunk = kTileBytes;          // 64 keys x 144 rows of bf16
+constexpr int kPBytes = 3 * kPChunk;         // keys 0-63, 64-127, 128-143 (+ unused tail)
 constexpr int kThreads = 256;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 160, kColO0 = 320, kColO1 = 384;
-constexpr int kNumBars = 17;
+constexpr uint32_t kColS = 0, kColS2 = 160, kColO0 = 320, kColO1 = 384, kColO2 = 448;
+constexpr int kNumBars = 18;
 constexpr int kSmem = kStages * kStageBytes + kPBytes + kNumBars * 8 + 16 + 1024;
 constexpr uint32_t kIdescS = ptx::make_idesc(1, 128, kMaxN, false, false);
 constexpr uint32_t kIdescO = ptx::make_idesc(1, 128, 64, false, true);
+constexpr uint32_t kRowOff16 = 16 * 128;  // 16 rows of a 128-byte-row tile (swizzle-atom aligned)
 
-// Barrier slots.
-enum { kFull = 0, kEmpty = 3, kSFull = 6, kSFree = 8, kPFull = 10, kPEmpty = 11, kOFull = 12, kOFree = 14,
-       kDone = 16 };
+enum { kFull = 0, kEmpty = 3, kSFull = 6, kSFree = 7, kPFull = 8, kPEmpty = 9, kOFull = 10, kOFree = 12,
+       kO2Full = 14, kO2Free = 15, kDone = 16 };
 
 // Masked keys of one row as a bit per key (bit j set = masked). Reads the window's region ids
 // (or the row of the u8 mask) 16 bytes at a time when N is a multiple of 16.
 __device__ __forceinline__ uint32_t nibble_of_bytes(uint32_t ne) {
-  // ne: 0xff per byte that marks a masked key -> 4 bits
   return (ne & 1u) | ((ne >> 7) & 2u) | ((ne >> 14) & 4u) | ((ne >> 21) & 8u);
 }
 
@@ -446,9 +448,7 @@ template <int kMask>
 __device__ __forceinline__ void row_mask_bits(const Params& p, int mw, int row, uint32_t bits[5]) {
 #pragma unroll
   for (int i = 0; i < 5; ++i) bits[i] = 0u;
-  if constexpr (kMask == kNoMask) {
-    return;
-  } else {
+  if constexpr (kMask != kNoMask) {
     const uint8_t* src;
     uint32_t ref = 0;
     if constexpr (kMask == kGroups) {
@@ -464,9 +464,8 @@ __device__ __forceinline__ void row_mask_bits(const Params& p, int mw, int row, 
         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const uint32_t ne = __vcmpne4(ws[k], ref);
-          const int j4 = 4 * v + k;  // word index: keys 4*j4 .. 4*j4+3
-          bits[j4 >> 3] |= nibble_of_bytes(ne) << ((j4 & 7) * 4);
+          const int j4 = 4 * v + k;
+          bits[j4 >> 3] |= nibble_of_bytes(__vcmpne4(ws[k], ref)) << ((j4 & 7) * 4);
         }
       }
     } else {
@@ -476,6 +475,87 @@ __device__ __forceinline__ void row_mask_bits(const Params& p, int mw, int row, 
         if (m) bits[key >> 5] |= 1u << (key & 31);
       }
     }
+  }
+}
+
+// One softmax row: S (144 fp32 in registers) -> P (bf16 pairs), returns the row sum. Max and
+// sum use 8 independent accumulators so the single warp per scheduler is not latency bound.
+template <int kMask>
+__device__ __forceinline__ float softmax_row(uint32_t (&sr)[9][16], uint32_t (&pk)[9][8], const uint32_t mbits[5],
+                                             float scale_log2, int N) {
+  float mx8[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
+  const uint32_t kMaskBits = __float_as_uint(kMaskedLog2);
+#pragma unroll
+  for (int c = 0; c < 9; ++c) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int key = 16 * c + e;
+      float y;
+      if constexpr (kMask != kNoMask) {
+        const uint32_t bit = (mbits[key >> 5] >> (key & 31)) & 1u;
+        y = fmaf(__uint_as_float(sr[c][e]), scale_log2, __uint_as_float((0u - bit) & kMaskBits));
+      } else {
+        y = __uint_as_float(sr[c][e]) * scale_log2;
+      }
+      if (key >= N) y = -INFINITY;
+      sr[c][e] = __float_as_uint(y);
+      mx8[e & 7] = fmaxf(mx8[e & 7], y);
+    }
+  }
+  const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                         fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+  float l8[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) l8[e] = 0.f;
+#pragma unroll
+  for (int c = 0; c < 9; ++c) {
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+      const float a = ex2(__uint_as_float(sr[c][e]) - mx);
+      const float b = ex2(__uint_as_float(sr[c][e + 1]) - mx);
+      l8[(e >> 1) & 7] += a + b;
+      pk[c][e >> 1] = pack_bf16x2(a, b);
+    }
+  }
+  return ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+}
+
+// P row `prow` (0..143) -> shared memory, UMMA A operand: K-major, 64-key chunks of 144 rows.
+__device__ __forceinline__ void store_p_row(uint32_t sP, int prow, const uint32_t (&pk)[9][8]) {
+#pragma unroll
+  for (int c = 0; c < 9; ++c) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int j16 = 2 * c + hh;  // 8-key group 0..17
+      const uint32_t addr = sP + (j16 >> 3) * kPChunk + prow * 128 + (((j16 & 7) ^ (prow & 7)) << 4);
+      st_shared_v4(addr, pk[c][4 * hh], pk[c][4 * hh + 1], pk[c][4 * hh + 2], pk[c][4 * hh + 3]);
+    }
+  }
+}
+
+// O row (64 fp32 in TMEM) * inv -> bf16 -> 128 contiguous bytes in global memory.
+__device__ __forceinline__ void store_o_row(uint32_t taddr, float inv, __nv_bfloat16* dst, bool valid) {
+  uint32_t o[4][16];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) tmem_ld16(taddr + 16 * c, o[c]);
+  tmem_wait_ld();
+  if (!valid) return;
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint4 a, b;
+    a.x = pack_bf16x2(__uint_as_float(o[c][0]) * inv, __uint_as_float(o[c][1]) * inv);
+    a.y = pack_bf16x2(__uint_as_float(o[c][2]) * inv, __uint_as_float(o[c][3]) * inv);
+    a.z = pack_bf16x2(__uint_as_float(o[c][4]) * inv, __uint_as_float(o[c][5]) * inv);
+    a.w = pack_bf16x2(__uint_as_float(o[c][6]) * inv, __uint_as_float(o[c][7]) * inv);
+    b.x = pack_bf16x2(__uint_as_float(o[c][8]) * inv, __uint_as_float(o[c][9]) * inv);
+    b.y = pack_bf16x2(__uint_as_float(o[c][10]) * inv, __uint_as_float(o[c][11]) * inv);
+    b.z = pack_bf16x2(__uint_as_float(o[c][12]) * inv, __uint_as_float(o[c][13]) * inv);
+    b.w = pack_bf16x2(__uint_as_float(o[c][14]) * inv, __uint_as_float(o[c][15]) * inv);
+    d[2 * c] = a;
+    d[2 * c + 1] = b;
   }
 }
 
@@ -498,16 +578,18 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
     abort_flag = 0;
     for (int s = 0; s < kStages; ++s) {
       mbar_init(BAR(kFull + s), 1);
-      mbar_init(BAR(kEmpty + s), 2);  // UMMA commit + remainder warp
+      mbar_init(BAR(kEmpty + s), 1);
     }
+    mbar_init(BAR(kSFull), 1);
+    mbar_init(BAR(kSFree), 5);  // 4 softmax warps + the rows-128..143 warp
+    mbar_init(BAR(kPFull), 5);
+    mbar_init(BAR(kPEmpty), 1);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(BAR(kSFull + b), 1);
-      mbar_init(BAR(kSFree + b), 4);
       mbar_init(BAR(kOFull + b), 1);
       mbar_init(BAR(kOFree + b), 4);
     }
-    mbar_init(BAR(kPFull), 4);
-    mbar_init(BAR(kPEmpty), 1);
+    mbar_init(BAR(kO2Full), 1);
+    mbar_init(BAR(kO2Free), 1);
     mbar_init(BAR(kDone), 1);
     fence_mbarrier_init();
   }
@@ -553,16 +635,19 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
         if (!mbar_wait(BAR(kPFull), (uint32_t)(j & 1), abort, p.status, 13, kTimeoutNs)) return false;
         if (!mbar_wait(BAR(kOFree + ob), (uint32_t)(((j >> 1) & 1) ^ 1), abort, p.status, 14, kTimeoutNs))
           return false;
+        if (!mbar_wait(BAR(kO2Free), (uint32_t)((j & 1) ^ 1), abort, p.status, 22, kTimeoutNs)) return false;
         tc_fence_after();
         const uint32_t sV = sbase + s * kStageBytes + 2 * kTileBytes;
         const uint32_t dO = tmem + (ob ? kColO1 : kColO0);
 #pragma unroll
         for (int k = 0; k < 9; ++k) {
-          const uint64_t a = desc_sw128(sP + (k >> 2) * kPChunk + (k & 3) * 32, 16, 1024);
+          const uint32_t pa = sP + (k >> 2) * kPChunk + (k & 3) * 32;
           const uint64_t b = desc_sw128(sV + k * 2048, kTileBytes, 1024);
-          umma_f16(dO, a, b, kIdescO, k > 0 ? 1u : 0u);
+          umma_f16(dO, desc_sw128(pa, 16, 1024), b, kIdescO, k > 0 ? 1u : 0u);
+          umma_f16(tmem + kColO2, desc_sw128(pa + kRowOff16, 16, 1024), b, kIdescO, k > 0 ? 1u : 0u);
         }
         umma_commit(BAR(kOFull + ob));
+        umma_commit(BAR(kO2Full));
         umma_commit(BAR(kPEmpty));
         umma_commit(BAR(kEmpty + s));
         return true;
@@ -570,16 +655,18 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       int i = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
-        const int s = i % kStages, sb = i & 1;
+        const int s = i % kStages;
         if (!mbar_wait(BAR(kFull + s), (uint32_t)((i / kStages) & 1), abort, p.status, 15, kTimeoutNs)) { ok = false; break; }
-        if (!mbar_wait(BAR(kSFree + sb), (uint32_t)(((i >> 1) & 1) ^ 1), abort, p.status, 16, kTimeoutNs)) { ok = false; break; }
+        if (!mbar_wait(BAR(kSFree), (uint32_t)((i & 1) ^ 1), abort, p.status, 16, kTimeoutNs)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sQ = sbase + s * kStageBytes, sK = sQ + kTileBytes;
-        const uint32_t dS = tmem + (sb ? kColS1 : kColS0);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma_f16(dS, desc_sw128(sQ + k * 32, 16, 1024), desc_sw128(sK + k * 32, 16, 1024), kIdescS, k > 0 ? 1u : 0u);
-        umma_commit(BAR(kSFull + sb));
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t b = desc_sw128(sK + k * 32, 16, 1024);
+          umma_f16(tmem + kColS, desc_sw128(sQ + k * 32, 16, 1024), b, kIdescS, k > 0 ? 1u : 0u);
+          umma_f16(tmem + kColS2, desc_sw128(sQ + kRowOff16 + k * 32, 16, 1024), b, kIdescS, k > 0 ? 1u : 0u);
+        }
+        umma_commit(BAR(kSFull));
         if (i > 0 && !issue_pv(i - 1)) { ok = false; break; }
       }
       if (ok && i > 0) issue_pv(i - 1);
@@ -587,130 +674,62 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       int no_abort = 0;
       mbar_wait(BAR(kDone), 0, &no_abort, p.status, 17, kTimeoutNs);
     }
-  } else if (warp == 2) {
-    // ---------------- rows 128..143 on mma.sync ----------------
-    int i = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
-      const int s = i % kStages;
-      if (!mbar_wait(BAR(kFull + s), (uint32_t)((i / kStages) & 1), abort, p.status, 18, kTimeoutNs)) break;
-      if (p.N > 128) {
-        const int w = t / p.H, h = t - w * p.H;
-        MaskView<kMask> mv;
-        mv.N = p.N;
-        const int mw = w % p.nW;
-        if constexpr (kMask == kGroups) mv.base = p.mask + (int64_t)mw * p.N;
-        else if constexpr (kMask == kMaskU8) mv.base = p.mask + (int64_t)mw * p.N * p.N;
-        else mv.base = nullptr;
-        const uint32_t st = sbase + s * kStageBytes;
-        rows16_bf16<kMask>(st, st + kTileBytes, st + 2 * kTileBytes, 128, p.N, p.scale_log2, mv,
-                           reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)w * p.os_w + (int64_t)h * p.os_h,
-                           p.os_n, lane);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kEmpty + s));
-    }
-  } else if (warp >= 4) {
-    // ---------------- softmax + epilogue, rows 0..127 ----------------
+  } else if (warp == 3 || warp >= 4) {
+    // ---------------- softmax + epilogue ----------------
+    // warps 4..7: rows 0..127 from S/O (lane quadrant warp & 3).
+    // warp 3:     rows 112..143 from S2/O2 lanes 96..127; only lanes 16..31 (rows 128..143) are kept.
+    const bool rem = warp == 3;
     const int q4 = warp & 3;
-    const int row = q4 * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    const int row = rem ? 112 + lane : q4 * 32 + lane;
+    const bool owner = !rem || lane >= 16;  // this thread writes its P/O row
+    const uint32_t colS = rem ? kColS2 : kColS;
     float l_prev = 1.f;
     int t_prev = -1, j_prev = -1;
 
     auto epilogue = [&](int j, int t, float l) -> bool {
       const int ob = j & 1;
-      if (!mbar_wait(BAR(kOFull + ob), (uint32_t)((j >> 1) & 1), abort, p.status, 19, kTimeoutNs)) return false;
+      const int fullbar = rem ? kO2Full : kOFull + ob;
+      const uint32_t par = rem ? (uint32_t)(j & 1) : (uint32_t)((j >> 1) & 1);
+      if (!mbar_wait(BAR(fullbar), par, abort, p.status, 19, kTimeoutNs)) return false;
       tc_fence_after();
-      uint32_t o[4][16];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld16(tmem + lane_addr + (ob ? kColO1 : kColO0) + 16 * c, o[c]);
-      tmem_wait_ld();
+      const int w = t / p.H, h = t - w * p.H;
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)w * p.os_w + (int64_t)h * p.os_h +
+                           (int64_t)row * p.os_n;
+      store_o_row(tmem + lane_addr + (rem ? kColO2 : (ob ? kColO1 : kColO0)), 1.f / l, dst, owner && row < p.N);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kOFree + ob));
-      if (row < p.N) {
-        const int w = t / p.H, h = t - w * p.H;
-        const float inv = 1.f / l;
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)w * p.os_w +
-                                              (int64_t)h * p.os_h + (int64_t)row * p.os_n);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint4 a, b;
-          a.x = pack_bf16x2(__uint_as_float(o[c][0]) * inv, __uint_as_float(o[c][1]) * inv);
-          a.y = pack_bf16x2(__uint_as_float(o[c][2]) * inv, __uint_as_float(o[c][3]) * inv);
-          a.z = pack_bf16x2(__uint_as_float(o[c][4]) * inv, __uint_as_float(o[c][5]) * inv);
-          a.w = pack_bf16x2(__uint_as_float(o[c][6]) * inv, __uint_as_float(o[c][7]) * inv);
-          b.x = pack_bf16x2(__uint_as_float(o[c][8]) * inv, __uint_as_float(o[c][9]) * inv);
-          b.y = pack_bf16x2(__uint_as_float(o[c][10]) * inv, __uint_as_float(o[c][11]) * inv);
-          b.z = pack_bf16x2(__uint_as_float(o[c][12]) * inv, __uint_as_float(o[c][13]) * inv);
-          b.w = pack_bf16x2(__uint_as_float(o[c][14]) * inv, __uint_as_float(o[c][15]) * inv);
-          dst[2 * c] = a;
-          dst[2 * c + 1] = b;
-        }
-      }
+      if (lane == 0) mbar_arrive(BAR(rem ? kO2Free : kOFree + ob));
       return true;
     };
 
     int i = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
-      const int sb = i & 1;
       const int w = t / p.H;
       uint32_t mbits[5];
       row_mask_bits<kMask>(p, w % p.nW, row, mbits);
-      if (!mbar_wait(BAR(kSFull + sb), (uint32_t)((i >> 1) & 1), abort, p.status, 20, kTimeoutNs)) { ok = false; break; }
+      if (!mbar_wait(BAR(kSFull), (uint32_t)(i & 1), abort, p.status, 20, kTimeoutNs)) { ok = false; break; }
       tc_fence_after();
       uint32_t sr[9][16];
 #pragma unroll
-      for (int c = 0; c < 9; ++c) tmem_ld16(tmem + lane_addr + (sb ? kColS1 : kColS0) + 16 * c, sr[c]);
+      for (int c = 0; c < 9; ++c) tmem_ld16(tmem + lane_addr + colS + 16 * c, sr[c]);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kSFree + sb));
-      // logits -> log2 domain, mask, row max
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 9; ++c) {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int key = 16 * c + e;
-          float y = __uint_as_float(sr[c][e]) * p.scale_log2;
-          if constexpr (kMask != kNoMask) {
-            if ((mbits[key >> 5] >> (key & 31)) & 1u) y += kMaskedLog2;
-          }
-          if (key >= p.N) y = -INFINITY;
-          sr[c][e] = __float_as_uint(y);
-          mx = fmaxf(mx, y);
-        }
+      if (lane == 0) mbar_arrive(BAR(kSFree));
+      if (rem && j_prev >= 0) {  // O2 is single-buffered: drain it before the next PV can start
+        if (!epilogue(j_prev, t_prev, l_prev)) { ok = false; break; }
+        j_prev = -1;
       }
-      float l = 0.f;
       uint32_t pk[9][8];
-#pragma unroll
-      for (int c = 0; c < 9; ++c) {
-#pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-          const float a = ex2(__uint_as_float(sr[c][e]) - mx);
-          const float b = ex2(__uint_as_float(sr[c][e + 1]) - mx);
-          l += a + b;
-          pk[c][e >> 1] = pack_bf16x2(a, b);
-        }
-      }
-      // P row -> shared memory (UMMA A operand, K-major, 128-byte swizzle, 64-key chunks).
+      const float l = softmax_row<kMask>(sr, pk, mbits, p.scale_log2, p.N);
       if (!mbar_wait(BAR(kPEmpty), (uint32_t)((i & 1) ^ 1), abort, p.status, 21, kTimeoutNs)) { ok = false; break; }
-#pragma unroll
-      for (int c = 0; c < 9; ++c) {
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int j16 = 2 * c + hh;            // 8-key group 0..17
-          const int chunk = j16 >> 3, jj = j16 & 7;
-          const uint32_t addr = sP + chunk * kPChunk + row * 128 + ((jj ^ (row & 7)) << 4);
-          st_shared_v4(addr, pk[c][4 * hh], pk[c][4 * hh + 1], pk[c][4 * hh + 2], pk[c][4 * hh + 3]);
-        }
-      }
+      if (owner) store_p_row(sP, rem ? row : row, pk);
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kPFull));
-      if (j_prev >= 0 && !epilogue(j_prev, t_prev, l_prev)) { ok = false; break; }
+      if (!rem && j_prev >= 0 && !epilogue(j_prev, t_prev, l_prev)) { ok = false; break; }
       j_prev = i;
       t_prev = t;
       l_prev = l;
