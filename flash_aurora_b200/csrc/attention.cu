@@ -407,18 +407,23 @@ attn_sync_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
 // query blocks through the tensor cores: rows 0..127 and rows 16..143 (the second block reuses
 // the same shared-memory tiles at a 16-row offset; only its last 16 rows, 128..143, are kept).
 //
-// Warp roles (256 threads, one CTA per SM, persistent over (window, head) tiles):
-//   warp 0      TMA producer: Q, K, V of a tile into a 3-stage ring (128-byte swizzle).
-//   warp 1      owns TMEM (512 columns) and, from one thread, issues the UMMAs:
-//                 S  = Q[0:128]  K^T, S2 = Q[16:144] K^T   (M=128, N=144, K=64, K-major A and B)
-//                 O  = P[0:128]  V,   O2 = P[16:144] V     (M=128, N=64, K=144, V MN-major)
-//               and signals completion with tcgen05.commit on mbarriers.
-//   warps 4..7  softmax + epilogue of rows 0..127: one TMEM lane (row) per thread; S row from TMEM,
-//               scale + mask + exp2 + row sum in fp32, P row (bf16) into shared memory in the UMMA
-//               A-operand layout; then O row from TMEM, times 1/sum, bf16, to global memory.
-//   warp 3      the same for rows 128..143, read from S2/O2 lanes 112..127 (its TMEM quadrant).
-// S is read into registers at the start of the softmax and released at once, so the S UMMAs of
-// tile i+1 run under the softmax of tile i; O is double-buffered. Every wait is bounded.
+// Warp roles (384 threads, one CTA per SM, persistent over a contiguous range of
+// (window, head) tiles, so consecutive tiles of a CTA are the heads of one window):
+//   warp 0       TMA producer: Q, K, V of a tile into a 3-stage ring (128-byte swizzle).
+//   warp 1       owns TMEM (512 columns) and, from one thread, issues the UMMAs:
+//                  S  = Q[0:128]  K^T, S2 = Q[16:144] K^T   (M=128, N=144, K=64, K-major A and B)
+//                  O  = P[0:128]  V,   O2 = P[16:144] V     (M=128, N=64, K=144, V MN-major)
+//                in whatever order their inputs become ready (non-blocking barrier tests),
+//                signalling completion with tcgen05.commit on mbarriers.
+//   warps 4..11  softmax + epilogue of rows 0..127: two warpgroups split every row, 72 key columns
+//                (and 32 output columns) each; the row max and row sum are exchanged through shared
+//                memory. S comes from TMEM (32x32b loads, one lane = one row per thread), P goes to
+//                shared memory as bf16 in the UMMA A-operand layout, O rows are scaled by 1/sum and
+//                written to global memory as bf16.
+//   warp 3       rows 128..143 from S2/O2 TMEM lanes 112..127 with 16x256b loads (16 rows spread
+//                over the 32 threads, two rows per thread, reductions over 4-thread quads).
+// The shifted-window mask is turned into a bit per key once per window and reused by its heads; a
+// window with a single region skips masking. Every wait is bounded (status word + abort flag).
 // ------------------------------------------------------------------------------------------
 namespace tc {
 
@@ -426,24 +431,25 @@ constexpr int kStages = 3;
 constexpr int kStageBytes = 3 * kTileBytes;  // Q, K, V (bf16, 144 x 128 B each)
 constexpr int kPChunk = kTileBytes;          // 64 keys x 144 rows of bf16
 constexpr int kPBytes = 3 * kPChunk;         // keys 0-63, 64-127, 128-143 (+ unused tail)
-constexpr int kThreads = 256;
+constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // {max, sum} x warpgroup x row
+constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColS2 = 160, kColO0 = 320, kColO1 = 384, kColO2 = 448;
-constexpr int kNumBars = 18;
-constexpr int kSmem = kStages * kStageBytes + kPBytes + kNumBars * 8 + 16 + 1024;
+constexpr int kNumBars = 20;
+constexpr int kSmem = kStages * kStageBytes + kPBytes + kXchgBytes + kNumBars * 8 + 16 + 1024;
 constexpr uint32_t kIdescS = ptx::make_idesc(1, 128, kMaxN, false, false);
 constexpr uint32_t kIdescO = ptx::make_idesc(1, 128, 64, false, true);
 constexpr uint32_t kRowOff16 = 16 * 128;  // 16 rows of a 128-byte-row tile (swizzle-atom aligned)
 
 enum { kFull = 0, kEmpty = 3, kSFull = 6, kSFree = 7, kPFull = 8, kPEmpty = 9, kOFull = 10, kOFree = 12,
-       kO2Full = 14, kO2Free = 15, kDone = 16 };
+       kO2Full = 14, kO2Free = 15, kDone = 16, kXMax = 17, kXSum = 18 };
 
-// Masked keys of one row as a bit per key (bit j set = masked). Reads the window's region ids
-// (or the row of the u8 mask) 16 bytes at a time when N is a multiple of 16.
 __device__ __forceinline__ uint32_t nibble_of_bytes(uint32_t ne) {
   return (ne & 1u) | ((ne >> 7) & 2u) | ((ne >> 14) & 4u) | ((ne >> 21) & 8u);
 }
 
+// Masked keys of one row as a bit per key (bit j set = masked), keys 0..143 in 5 words. Reads the
+// window's region ids (or the row of the u8 mask) 16 bytes at a time when N is a multiple of 16.
 template <int kMask>
 __device__ __forceinline__ void row_mask_bits(const Params& p, int mw, int row, uint32_t bits[5]) {
 #pragma unroll
@@ -478,85 +484,46 @@ __device__ __forceinline__ void row_mask_bits(const Params& p, int mw, int row, 
   }
 }
 
-// One softmax row: S (144 fp32 in registers) -> P (bf16 pairs), returns the row sum. Max and
-// sum use 8 independent accumulators so the single warp per scheduler is not latency bound.
-template <int kMask>
-__device__ __forceinline__ float softmax_row(uint32_t (&sr)[9][16], uint32_t (&pk)[9][8], const uint32_t mbits[5],
-                                             float scale_log2, int N) {
-  float mx8[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
-  const uint32_t kMaskBits = __float_as_uint(kMaskedLog2);
-#pragma unroll
-  for (int c = 0; c < 9; ++c) {
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int key = 16 * c + e;
-      float y;
-      if constexpr (kMask != kNoMask) {
-        const uint32_t bit = (mbits[key >> 5] >> (key & 31)) & 1u;
-        y = fmaf(__uint_as_float(sr[c][e]), scale_log2, __uint_as_float((0u - bit) & kMaskBits));
-      } else {
-        y = __uint_as_float(sr[c][e]) * scale_log2;
-      }
-      if (key >= N) y = -INFINITY;
-      sr[c][e] = __float_as_uint(y);
-      mx8[e & 7] = fmaxf(mx8[e & 7], y);
-    }
-  }
-  const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                         fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-  float l8[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) l8[e] = 0.f;
-#pragma unroll
-  for (int c = 0; c < 9; ++c) {
-#pragma unroll
-    for (int e = 0; e < 16; e += 2) {
-      const float a = ex2(__uint_as_float(sr[c][e]) - mx);
-      const float b = ex2(__uint_as_float(sr[c][e + 1]) - mx);
-      l8[(e >> 1) & 7] += a + b;
-      pk[c][e >> 1] = pack_bf16x2(a, b);
-    }
-  }
-  return ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
-}
-
-// P row `prow` (0..143) -> shared memory, UMMA A operand: K-major, 64-key chunks of 144 rows.
-__device__ __forceinline__ void store_p_row(uint32_t sP, int prow, const uint32_t (&pk)[9][8]) {
-#pragma unroll
-  for (int c = 0; c < 9; ++c) {
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int j16 = 2 * c + hh;  // 8-key group 0..17
-      const uint32_t addr = sP + (j16 >> 3) * kPChunk + prow * 128 + (((j16 & 7) ^ (prow & 7)) << 4);
-      st_shared_v4(addr, pk[c][4 * hh], pk[c][4 * hh + 1], pk[c][4 * hh + 2], pk[c][4 * hh + 3]);
-    }
-  }
-}
-
-// O row (64 fp32 in TMEM) * inv -> bf16 -> 128 contiguous bytes in global memory.
-__device__ __forceinline__ void store_o_row(uint32_t taddr, float inv, __nv_bfloat16* dst, bool valid) {
-  uint32_t o[4][16];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) tmem_ld16(taddr + 16 * c, o[c]);
+// 72 consecutive TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld72(uint32_t taddr, uint32_t (&v)[72]) {
+  uint32_t a[16], b[16], c[16], d[16], e[8];
+  tmem_ld16(taddr, a);
+  tmem_ld16(taddr + 16, b);
+  tmem_ld16(taddr + 32, c);
+  tmem_ld16(taddr + 48, d);
+  tmem_ld8(taddr + 64, e);
   tmem_wait_ld();
-  if (!valid) return;
-  uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint4 a, b;
-    a.x = pack_bf16x2(__uint_as_float(o[c][0]) * inv, __uint_as_float(o[c][1]) * inv);
-    a.y = pack_bf16x2(__uint_as_float(o[c][2]) * inv, __uint_as_float(o[c][3]) * inv);
-    a.z = pack_bf16x2(__uint_as_float(o[c][4]) * inv, __uint_as_float(o[c][5]) * inv);
-    a.w = pack_bf16x2(__uint_as_float(o[c][6]) * inv, __uint_as_float(o[c][7]) * inv);
-    b.x = pack_bf16x2(__uint_as_float(o[c][8]) * inv, __uint_as_float(o[c][9]) * inv);
-    b.y = pack_bf16x2(__uint_as_float(o[c][10]) * inv, __uint_as_float(o[c][11]) * inv);
-    b.z = pack_bf16x2(__uint_as_float(o[c][12]) * inv, __uint_as_float(o[c][13]) * inv);
-    b.w = pack_bf16x2(__uint_as_float(o[c][14]) * inv, __uint_as_float(o[c][15]) * inv);
-    d[2 * c] = a;
-    d[2 * c + 1] = b;
+  for (int i = 0; i < 16; ++i) {
+    v[i] = a[i];
+    v[16 + i] = b[i];
+    v[32 + i] = c[i];
+    v[48 + i] = d[i];
   }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[64 + i] = e[i];
+}
+
+// Logits of 72 keys in the raw (unscaled) domain: s, plus -100/scale where masked, -inf past N.
+template <bool kMasked, bool kFullN>
+__device__ __forceinline__ float raw_logits72(uint32_t (&v)[72], const uint32_t rel[3], float braw, int kbase,
+                                              int N) {
+  float mx[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) mx[e] = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < 72; ++k) {
+    float y = __uint_as_float(v[k]);
+    if constexpr (kMasked) {
+      if ((rel[k >> 5] >> (k & 31)) & 1u) y += braw;
+    }
+    if constexpr (!kFullN) {
+      if (kbase + k >= N) y = -INFINITY;
+    }
+    v[k] = __float_as_uint(y);
+    mx[k & 7] = fmaxf(mx[k & 7], y);
+  }
+  return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
 }
 
 template <int kMask>
@@ -567,11 +534,17 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t sP = sbase + kStages * kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kPBytes);
+  float* xchg = reinterpret_cast<float*>(smem + kStages * kStageBytes + kPBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kPBytes + kXchgBytes);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
   const uint32_t bar0 = smem_u32(bars);
   auto BAR = [&](int slot) -> uint32_t { return bar0 + 8u * (uint32_t)slot; };
   __shared__ int abort_flag;
+
+  // Contiguous tile range of this CTA (heads of a window are consecutive tiles).
+  const int t_begin = (int)(((int64_t)blockIdx.x * p.num_tiles) / gridDim.x);
+  const int t_end = (int)(((int64_t)(blockIdx.x + 1) * p.num_tiles) / gridDim.x);
+  const int n_local = t_end - t_begin;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -581,16 +554,18 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       mbar_init(BAR(kEmpty + s), 1);
     }
     mbar_init(BAR(kSFull), 1);
-    mbar_init(BAR(kSFree), 5);  // 4 softmax warps + the rows-128..143 warp
-    mbar_init(BAR(kPFull), 5);
+    mbar_init(BAR(kSFree), 9);  // 8 softmax warps + the rows-128..143 warp
+    mbar_init(BAR(kPFull), 9);
     mbar_init(BAR(kPEmpty), 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR(kOFull + b), 1);
-      mbar_init(BAR(kOFree + b), 4);
+      mbar_init(BAR(kOFree + b), 8);
     }
     mbar_init(BAR(kO2Full), 1);
     mbar_init(BAR(kO2Free), 1);
     mbar_init(BAR(kDone), 1);
+    mbar_init(BAR(kXMax), 8);  // row-max exchange between the two softmax warpgroups
+    mbar_init(BAR(kXSum), 8);  // row-sum exchange
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -602,6 +577,8 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   volatile int* abort = &abort_flag;
+  const bool full_n = p.N == kMaxN;
+  const float braw = kMaskedLog2 / p.scale_log2;  // -100 / scale: the mask bias before scaling
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -610,8 +587,8 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
       int last_par[kStages] = {-1, -1, -1};
-      int i = 0;
-      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
+      for (int i = 0; i < n_local; ++i) {
+        const int t = t_begin + i;
         const int s = i % kStages;
         const uint32_t ph = (uint32_t)((i / kStages) & 1);
         if (!mbar_wait(BAR(kEmpty + s), ph ^ 1u, abort, p.status, 11, kTimeoutNs)) break;
@@ -628,113 +605,337 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
         if (last_par[s] >= 0) mbar_wait(BAR(kFull + s), (uint32_t)last_par[s], &no_abort, p.status, 12, kTimeoutNs);
     }
   } else if (warp == 1) {
-    // ---------------- UMMA issuer ----------------
+    // ---------------- UMMA issuer (event loop) ----------------
     if (lane == 0) {
-      auto issue_pv = [&](int j) -> bool {
-        const int s = j % kStages, ob = j & 1;
-        if (!mbar_wait(BAR(kPFull), (uint32_t)(j & 1), abort, p.status, 13, kTimeoutNs)) return false;
-        if (!mbar_wait(BAR(kOFree + ob), (uint32_t)(((j >> 1) & 1) ^ 1), abort, p.status, 14, kTimeoutNs))
-          return false;
-        if (!mbar_wait(BAR(kO2Free), (uint32_t)((j & 1) ^ 1), abort, p.status, 22, kTimeoutNs)) return false;
-        tc_fence_after();
-        const uint32_t sV = sbase + s * kStageBytes + 2 * kTileBytes;
-        const uint32_t dO = tmem + (ob ? kColO1 : kColO0);
+      int ns = 0, npv = 0;
+      uint64_t t_last = cycles();
+      uint32_t idle = 0;
+      while (npv < n_local) {
+        bool progressed = false;
+        if (ns < n_local) {
+          const int s = ns % kStages;
+          if (mbar_test_wait(BAR(kFull + s), (uint32_t)((ns / kStages) & 1)) &&
+              mbar_test_wait(BAR(kSFree), (uint32_t)((ns & 1) ^ 1))) {
+            tc_fence_after();
+            const uint32_t sQ = sbase + s * kStageBytes, sK = sQ + kTileBytes;
 #pragma unroll
-        for (int k = 0; k < 9; ++k) {
-          const uint32_t pa = sP + (k >> 2) * kPChunk + (k & 3) * 32;
-          const uint64_t b = desc_sw128(sV + k * 2048, kTileBytes, 1024);
-          umma_f16(dO, desc_sw128(pa, 16, 1024), b, kIdescO, k > 0 ? 1u : 0u);
-          umma_f16(tmem + kColO2, desc_sw128(pa + kRowOff16, 16, 1024), b, kIdescO, k > 0 ? 1u : 0u);
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t b = desc_sw128(sK + k * 32, 16, 1024);
+              umma_f16(tmem + kColS, desc_sw128(sQ + k * 32, 16, 1024), b, kIdescS, k > 0 ? 1u : 0u);
+              umma_f16(tmem + kColS2, desc_sw128(sQ + kRowOff16 + k * 32, 16, 1024), b, kIdescS, k > 0 ? 1u : 0u);
+            }
+            umma_commit(BAR(kSFull));
+            ++ns;
+            progressed = true;
+          }
         }
-        umma_commit(BAR(kOFull + ob));
-        umma_commit(BAR(kO2Full));
-        umma_commit(BAR(kPEmpty));
-        umma_commit(BAR(kEmpty + s));
-        return true;
-      };
-      int i = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
-        const int s = i % kStages;
-        if (!mbar_wait(BAR(kFull + s), (uint32_t)((i / kStages) & 1), abort, p.status, 15, kTimeoutNs)) { ok = false; break; }
-        if (!mbar_wait(BAR(kSFree), (uint32_t)((i & 1) ^ 1), abort, p.status, 16, kTimeoutNs)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t sQ = sbase + s * kStageBytes, sK = sQ + kTileBytes;
+        if (npv < ns) {
+          const int j = npv, s = j % kStages, ob = j & 1;
+          if (mbar_test_wait(BAR(kPFull), (uint32_t)(j & 1)) &&
+              mbar_test_wait(BAR(kOFree + ob), (uint32_t)(((j >> 1) & 1) ^ 1)) &&
+              mbar_test_wait(BAR(kO2Free), (uint32_t)((j & 1) ^ 1))) {
+            tc_fence_after();
+            const uint32_t sV = sbase + s * kStageBytes + 2 * kTileBytes;
+            const uint32_t dO = tmem + (ob ? kColO1 : kColO0);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t b = desc_sw128(sK + k * 32, 16, 1024);
-          umma_f16(tmem + kColS, desc_sw128(sQ + k * 32, 16, 1024), b, kIdescS, k > 0 ? 1u : 0u);
-          umma_f16(tmem + kColS2, desc_sw128(sQ + kRowOff16 + k * 32, 16, 1024), b, kIdescS, k > 0 ? 1u : 0u);
+            for (int k = 0; k < 9; ++k) {
+              const uint32_t pa = sP + (k >> 2) * kPChunk + (k & 3) * 32;
+              const uint64_t b = desc_sw128(sV + k * 2048, kTileBytes, 1024);
+              umma_f16(dO, desc_sw128(pa, 16, 1024), b, kIdescO, k > 0 ? 1u : 0u);
+              umma_f16(tmem + kColO2, desc_sw128(pa + kRowOff16, 16, 1024), b, kIdescO, k > 0 ? 1u : 0u);
+            }
+            umma_commit(BAR(kOFull + ob));
+            umma_commit(BAR(kO2Full));
+            umma_commit(BAR(kPEmpty));
+            umma_commit(BAR(kEmpty + s));
+            ++npv;
+            progressed = true;
+          }
         }
-        umma_commit(BAR(kSFull));
-        if (i > 0 && !issue_pv(i - 1)) { ok = false; break; }
+        if (progressed) {
+          idle = 0;
+          t_last = cycles();
+        } else if ((++idle & 63u) == 0) {
+          if (*abort) break;
+          if (cycles() - t_last > ns_to_cycles(kTimeoutNs)) {
+            atomicCAS(p.status, 0, 16);
+            *abort = 1;
+            break;
+          }
+        }
       }
-      if (ok && i > 0) issue_pv(i - 1);
       umma_commit(BAR(kDone));
       int no_abort = 0;
       mbar_wait(BAR(kDone), 0, &no_abort, p.status, 17, kTimeoutNs);
     }
-  } else if (warp == 3 || warp >= 4) {
-    // ---------------- softmax + epilogue ----------------
-    // warps 4..7: rows 0..127 from S/O (lane quadrant warp & 3).
-    // warp 3:     rows 112..143 from S2/O2 lanes 96..127; only lanes 16..31 (rows 128..143) are kept.
-    const bool rem = warp == 3;
+  } else if (warp >= 4) {
+    // ---------------- rows 0..127: softmax + epilogue, two warpgroups per row ----------------
+    const int g = (warp - 4) >> 2;  // key half: columns 72g .. 72g+71, output columns 32g .. 32g+31
     const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
-    const int row = rem ? 112 + lane : q4 * 32 + lane;
-    const bool owner = !rem || lane >= 16;  // this thread writes its P/O row
-    const uint32_t colS = rem ? kColS2 : kColS;
+    float* xmax = xchg;        // [2][128]
+    float* xsum = xchg + 256;  // [2][128]
+    int cached_w = -1;
+    uint32_t rel[3] = {0u, 0u, 0u};
+    bool wmask = false;
     float l_prev = 1.f;
     int t_prev = -1, j_prev = -1;
 
     auto epilogue = [&](int j, int t, float l) -> bool {
       const int ob = j & 1;
-      const int fullbar = rem ? kO2Full : kOFull + ob;
-      const uint32_t par = rem ? (uint32_t)(j & 1) : (uint32_t)((j >> 1) & 1);
-      if (!mbar_wait(BAR(fullbar), par, abort, p.status, 19, kTimeoutNs)) return false;
+      if (!mbar_wait(BAR(kOFull + ob), (uint32_t)((j >> 1) & 1), abort, p.status, 19, kTimeoutNs)) return false;
       tc_fence_after();
-      const int w = t / p.H, h = t - w * p.H;
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)w * p.os_w + (int64_t)h * p.os_h +
-                           (int64_t)row * p.os_n;
-      store_o_row(tmem + lane_addr + (rem ? kColO2 : (ob ? kColO1 : kColO0)), 1.f / l, dst, owner && row < p.N);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(rem ? kO2Free : kOFree + ob));
-      return true;
-    };
-
-    int i = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
-      const int w = t / p.H;
-      uint32_t mbits[5];
-      row_mask_bits<kMask>(p, w % p.nW, row, mbits);
-      if (!mbar_wait(BAR(kSFull), (uint32_t)(i & 1), abort, p.status, 20, kTimeoutNs)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t sr[9][16];
-#pragma unroll
-      for (int c = 0; c < 9; ++c) tmem_ld16(tmem + lane_addr + colS + 16 * c, sr[c]);
+      uint32_t o0[16], o1[16];
+      const uint32_t ta = tmem + lane_addr + (ob ? kColO1 : kColO0) + 32 * g;
+      tmem_ld16(ta, o0);
+      tmem_ld16(ta + 16, o1);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kSFree));
-      if (rem && j_prev >= 0) {  // O2 is single-buffered: drain it before the next PV can start
-        if (!epilogue(j_prev, t_prev, l_prev)) { ok = false; break; }
-        j_prev = -1;
+      if (lane == 0) mbar_arrive(BAR(kOFree + ob));
+      if (row < p.N) {
+        const int w = t / p.H, h = t - w * p.H;
+        const float inv = 1.f / l;
+        uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)w * p.os_w +
+                                            (int64_t)h * p.os_h + (int64_t)row * p.os_n + 32 * g);
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          pk[e] = pack_bf16x2(__uint_as_float(o0[2 * e]) * inv, __uint_as_float(o0[2 * e + 1]) * inv);
+          pk[8 + e] = pack_bf16x2(__uint_as_float(o1[2 * e]) * inv, __uint_as_float(o1[2 * e + 1]) * inv);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) d[c] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       }
-      uint32_t pk[9][8];
-      const float l = softmax_row<kMask>(sr, pk, mbits, p.scale_log2, p.N);
+      return true;
+    };
+
+    bool ok = true;
+    for (int i = 0; i < n_local; ++i) {
+      const int t = t_begin + i;
+      if constexpr (kMask != kNoMask) {
+        const int w = t / p.H;
+        if (w != cached_w) {
+          uint32_t b[5];
+          row_mask_bits<kMask>(p, w % p.nW, row, b);
+          cached_w = w;
+          wmask = (b[0] | b[1] | b[2] | b[3] | b[4]) != 0u;
+          // bits of keys 72g .. 72g+71
+          const uint32_t w0 = g ? b[2] : b[0], w1 = g ? b[3] : b[1], w2 = g ? b[4] : b[2];
+          const uint32_t w3 = g ? 0u : b[3];
+          const uint32_t sh = g ? 8u : 0u;
+          rel[0] = __funnelshift_r(w0, w1, sh);
+          rel[1] = __funnelshift_r(w1, w2, sh);
+          rel[2] = __funnelshift_r(w2, w3, sh) & 0xffu;
+        }
+      }
+      if (!mbar_wait(BAR(kSFull), (uint32_t)(i & 1), abort, p.status, 20, kTimeoutNs)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t v[72];
+      tmem_ld72(tmem + lane_addr + kColS + 72 * g, v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kSFree));
+      float pm;
+      if (full_n) pm = wmask ? raw_logits72<true, true>(v, rel, braw, 72 * g, p.N)
+                             : raw_logits72<false, true>(v, rel, braw, 72 * g, p.N);
+      else pm = wmask ? raw_logits72<true, false>(v, rel, braw, 72 * g, p.N)
+                      : raw_logits72<false, false>(v, rel, braw, 72 * g, p.N);
+      // Each slot is rewritten only after the partner passed the other exchange barrier of the
+      // same tile, so one slot per value suffices.
+      xmax[g * 128 + row] = pm;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kXMax));
+      if (!mbar_wait(BAR(kXMax), (uint32_t)(i & 1), abort, p.status, 24, kTimeoutNs)) { ok = false; break; }
+      const float m = fmaxf(pm, xmax[(g ^ 1) * 128 + row]);
+      const float c = p.scale_log2, mc = -m * c;
+      uint32_t pk[36];
+      float l8[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < 72; k += 2) {
+        const float a = ex2(fmaf(__uint_as_float(v[k]), c, mc));
+        const float b = ex2(fmaf(__uint_as_float(v[k + 1]), c, mc));
+        l8[(k >> 1) & 3] += a + b;
+        pk[k >> 1] = pack_bf16x2(a, b);
+      }
+      const float pl = (l8[0] + l8[1]) + (l8[2] + l8[3]);
+      xsum[g * 128 + row] = pl;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kXSum));
+      if (!mbar_wait(BAR(kXSum), (uint32_t)(i & 1), abort, p.status, 25, kTimeoutNs)) { ok = false; break; }
+      const float l = pl + xsum[(g ^ 1) * 128 + row];
       if (!mbar_wait(BAR(kPEmpty), (uint32_t)((i & 1) ^ 1), abort, p.status, 21, kTimeoutNs)) { ok = false; break; }
-      if (owner) store_p_row(sP, rem ? row : row, pk);
+#pragma unroll
+      for (int jj = 0; jj < 9; ++jj) {
+        const int j16 = 9 * g + jj;  // 8-key group 0..17
+        const uint32_t addr = sP + (j16 >> 3) * kPChunk + row * 128 + (((j16 & 7) ^ (row & 7)) << 4);
+        st_shared_v4(addr, pk[4 * jj], pk[4 * jj + 1], pk[4 * jj + 2], pk[4 * jj + 3]);
+      }
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kPFull));
-      if (!rem && j_prev >= 0 && !epilogue(j_prev, t_prev, l_prev)) { ok = false; break; }
+      if (j_prev >= 0 && !epilogue(j_prev, t_prev, l_prev)) { ok = false; break; }
       j_prev = i;
       t_prev = t;
       l_prev = l;
     }
     if (ok && j_prev >= 0) epilogue(j_prev, t_prev, l_prev);
+  } else if (warp == 3) {
+    // ---------------- rows 128..143 (S2/O2 lanes 112..127, 16x256b) ----------------
+    const int t0 = lane & 3, t1 = lane >> 2;
+    const int ra = 128 + t1, rb = 136 + t1;
+    const uint32_t lane_addr = 112u << 16;
+    int cached_w = -1;
+    uint32_t ta = 0, tb = 0, kp[18];
+    bool wmask = false;
+#pragma unroll
+    for (int j = 0; j < 18; ++j) kp[j] = 0u;
+    float la_prev = 1.f, lb_prev = 1.f;
+    int t_prev = -1, j_prev = -1;
+
+    auto epilogue_rem = [&](int j, int t, float la, float lb) -> bool {
+      if (!mbar_wait(BAR(kO2Full), (uint32_t)(j & 1), abort, p.status, 23, kTimeoutNs)) return false;
+      tc_fence_after();
+      uint32_t o[32];
+      tmem_ld_16x256b_r32(tmem + lane_addr + kColO2, o);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kO2Free));
+      const int w = t / p.H, h = t - w * p.H;
+      __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)w * p.os_w + (int64_t)h * p.os_h;
+      const float ia = 1.f / la, ib = 1.f / lb;
+      if (ra < p.N) {
+        uint32_t* d = reinterpret_cast<uint32_t*>(base + (int64_t)ra * p.os_n + 2 * t0);
+#pragma unroll
+        for (int jd = 0; jd < 8; ++jd)
+          d[4 * jd] = pack_bf16x2(__uint_as_float(o[4 * jd]) * ia, __uint_as_float(o[4 * jd + 1]) * ia);
+      }
+      if (rb < p.N) {
+        uint32_t* d = reinterpret_cast<uint32_t*>(base + (int64_t)rb * p.os_n + 2 * t0);
+#pragma unroll
+        for (int jd = 0; jd < 8; ++jd)
+          d[4 * jd] = pack_bf16x2(__uint_as_float(o[4 * jd + 2]) * ib, __uint_as_float(o[4 * jd + 3]) * ib);
+      }
+      return true;
+    };
+
+    bool ok = true;
+    for (int i = 0; i < n_local; ++i) {
+      const int t = t_begin + i;
+      if constexpr (kMask != kNoMask) {
+        const int w = t / p.H;
+        if (w != cached_w) {
+          cached_w = w;
+          const int mw = w % p.nW;
+          if constexpr (kMask == kGroups) {
+            const uint8_t* gi = p.mask + (int64_t)mw * p.N;
+            ta = ra < p.N ? __ldg(gi + ra) : 0u;
+            tb = rb < p.N ? __ldg(gi + rb) : 0u;
+            uint32_t any = 0;
+#pragma unroll
+            for (int j = 0; j < 18; ++j) {
+              const int key = 8 * j + 2 * t0;
+              const uint32_t lo = key < p.N ? __ldg(gi + key) : ta;
+              const uint32_t hi = key + 1 < p.N ? __ldg(gi + key + 1) : ta;
+              kp[j] = lo | (hi << 8);
+              any |= (lo != ta) | (hi != ta) | (lo != tb) | (hi != tb);
+            }
+            // A window with one region has no masked pair; this is uniform over the window.
+            wmask = __any_sync(0xffffffffu, any != 0u);
+          } else {
+            wmask = true;
+          }
+        }
+      }
+      if (!mbar_wait(BAR(kSFull), (uint32_t)(i & 1), abort, p.status, 20, kTimeoutNs)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t v[72];
+      {
+        uint32_t a[64], b[8];
+        tmem_ld_16x256b_r64(tmem + lane_addr + kColS2, a);
+        tmem_ld_16x256b_r8(tmem + lane_addr + kColS2 + 128, b);
+        tmem_wait_ld();
+#pragma unroll
+        for (int k = 0; k < 64; ++k) v[k] = a[k];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[64 + k] = b[k];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kSFree));
+      if (j_prev >= 0) {  // O2 is single-buffered: drain it before the next PV can start
+        if (!epilogue_rem(j_prev, t_prev, la_prev, lb_prev)) { ok = false; break; }
+        j_prev = -1;
+      }
+      // v[4j + {0,1}] = row ra, keys 8j + 2t0 + {0,1}; v[4j + {2,3}] = row rb, same keys.
+      float mxa = -INFINITY, mxb = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 18; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = 8 * j + 2 * t0 + e;
+          float ya = __uint_as_float(v[4 * j + e]), yb = __uint_as_float(v[4 * j + 2 + e]);
+          if constexpr (kMask == kGroups) {
+            if (wmask) {
+              const uint32_t kg = (kp[j] >> (8 * e)) & 0xffu;
+              if (kg != ta) ya += braw;
+              if (kg != tb) yb += braw;
+            }
+          } else if constexpr (kMask == kMaskU8) {
+            const uint8_t* mr = p.mask + (int64_t)(cached_w % p.nW) * p.N * p.N;
+            if (key < p.N && ra < p.N && __ldg(mr + (int64_t)ra * p.N + key)) ya += braw;
+            if (key < p.N && rb < p.N && __ldg(mr + (int64_t)rb * p.N + key)) yb += braw;
+          }
+          if (key >= p.N) {
+            ya = -INFINITY;
+            yb = -INFINITY;
+          }
+          v[4 * j + e] = __float_as_uint(ya);
+          v[4 * j + 2 + e] = __float_as_uint(yb);
+          mxa = fmaxf(mxa, ya);
+          mxb = fmaxf(mxb, yb);
+        }
+      }
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
+      const float c = p.scale_log2, mca = -mxa * c, mcb = -mxb * c;
+      float la = 0.f, lb = 0.f;
+      uint32_t pa[18], pb[18];
+#pragma unroll
+      for (int j = 0; j < 18; ++j) {
+        const float a0 = ex2(fmaf(__uint_as_float(v[4 * j]), c, mca));
+        const float a1 = ex2(fmaf(__uint_as_float(v[4 * j + 1]), c, mca));
+        const float b0 = ex2(fmaf(__uint_as_float(v[4 * j + 2]), c, mcb));
+        const float b1 = ex2(fmaf(__uint_as_float(v[4 * j + 3]), c, mcb));
+        la += a0 + a1;
+        lb += b0 + b1;
+        pa[j] = pack_bf16x2(a0, a1);
+        pb[j] = pack_bf16x2(b0, b1);
+      }
+      la += __shfl_xor_sync(0xffffffffu, la, 1);
+      la += __shfl_xor_sync(0xffffffffu, la, 2);
+      lb += __shfl_xor_sync(0xffffffffu, lb, 1);
+      lb += __shfl_xor_sync(0xffffffffu, lb, 2);
+      if (!mbar_wait(BAR(kPEmpty), (uint32_t)((i & 1) ^ 1), abort, p.status, 21, kTimeoutNs)) { ok = false; break; }
+#pragma unroll
+      for (int j = 0; j < 18; ++j) {
+        const uint32_t off = (j >> 3) * kPChunk + (uint32_t)(4 * t0);
+        st_shared_u32(sP + off + ra * 128 + (((j & 7) ^ (ra & 7)) << 4), pa[j]);
+        st_shared_u32(sP + off + rb * 128 + (((j & 7) ^ (rb & 7)) << 4), pb[j]);
+      }
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kPFull));
+      j_prev = i;
+      t_prev = t;
+      la_prev = la;
+      lb_prev = lb;
+    }
+    if (ok && j_prev >= 0) epilogue_rem(j_prev, t_prev, la_prev, lb_prev);
   }
   tc_fence_before();
   __syncthreads();
