@@ -39,6 +39,8 @@ SIGNATURES = {
     "fa_shifted_window_groups": (_i32, [_i64, _i64, _i64, _i32p, _i32p, _i32, _u8p]),
     "fa_window_attention": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64p, _u8p, _u8p, _i64, _f32, _vp]),
     "fa_window_attention_qkvpacked": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _u8p, _u8p, _i64, _f32, _vp]),
+    "fa_window_attention_bias_noalloc": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64p, _vp,
+                                                 _i64, _f32, _vp]),
     "fa_attention_status": (_i32, [ctypes.POINTER(ctypes.c_int)]),
     "fa_attention_status_reset": (_i32, [_vp]),
 }

@@ -25,5 +25,12 @@ struct Params {
 
 int* status_ptr();
 
+// Window attention on (Bwin, H, N, Dh) tensors with element strides {q, k, v, out} x
+// {window, head, token}; at most one of mask_u8 (nW, N, N) / group_ids (nW, N). Host entry of the
+// kernels in attention.cu; allocates nothing.
+int run(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const void* q, const void* k,
+        const void* v, void* out, const int64_t* strides, const uint8_t* mask_u8, const uint8_t* group_ids,
+        int64_t nW, float scale, void* stream);
+
 }  // namespace attn
 }  // namespace fa

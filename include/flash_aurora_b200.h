@@ -137,6 +137,21 @@ int fa_window_attention_qkvpacked(int precision, int64_t Bwin, int64_t N, int64_
                                   float scale, void* stream);
 
 /*
+ * fa_window_attention with a float bias (nW, N, N) (bias < -50 means masked, as upstream) that
+ * allocates no device memory. No counterpart in the reference: it exists for callers that cannot
+ * call cudaMalloc (a host that owns the memory pool, a plugin forbidden to allocate, a loop that must
+ * not allocate after start-up). The packed mask goes to a static 4 MiB device array of this
+ * library, so nW * N * N must be <= 4194304 (larger sizes return FA_ERR_INVALID). The array's
+ * device address is looked up on the first call on each device (call it once before any stream
+ * capture). All calls share the array: calls that overlap on the GPU (other streams, other host
+ * threads) race on it; serialise them. The caller still passes q, k, v, out and bias.
+ */
+int fa_window_attention_bias_noalloc(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh,
+                                     const void* q, const void* k, const void* v, void* out,
+                                     const int64_t strides[12], const float* bias, int64_t nW,
+                                     float scale, void* stream);
+
+/*
  * Device status word of the attention kernels: 0 when every bounded wait of every launch since
  * the last reset completed, else the code of the first wait that gave up. Synchronises the
  * device. fa_attention_status_reset clears it (stream-ordered).
