@@ -404,15 +404,17 @@ attn_sync_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
 // BF16 kernel on the 5th-generation tensor cores (tcgen05 / UMMA, accumulators in TMEM).
 //
 // A window has 144 query rows; an M=128 UMMA covers 128. Every tile therefore runs two
-// query blocks through the tensor cores: rows 0..127 and rows 16..143 (the second block reuses
-// the same shared-memory tiles at a 16-row offset; only its last 16 rows, 128..143, are kept).
+// query blocks through the tensor cores: rows 0..127 (M=128) and rows 80..143 (M=64, reusing the
+// same shared-memory tiles at an 80-row offset; only its last 16 rows, 128..143, are kept). An M=64
+// accumulator fills half of the TMEM lanes, so two of them (O2 of consecutive tiles) share columns.
 //
 // Warp roles (384 threads, one CTA per SM, persistent over a contiguous range of
 // (window, head) tiles, so consecutive tiles of a CTA are the heads of one window):
-//   warp 0       TMA producer: Q, K, V of a tile into a 3-stage ring (128-byte swizzle).
+//   warps 0, 2   TMA producers: Q and K (warp 0) and V (warp 2) of a tile into 3-slot rings
+//                (128-byte swizzle); Q/K slots are freed when the S UMMAs finish, V slots after PV.
 //   warp 1       owns TMEM (512 columns) and, from one thread, issues the UMMAs:
-//                  S  = Q[0:128]  K^T, S2 = Q[16:144] K^T   (M=128, N=144, K=64, K-major A and B)
-//                  O  = P[0:128]  V,   O2 = P[16:144] V     (M=128, N=64, K=144, V MN-major)
+//                  S  = Q[0:128]  K^T (M=128), S2 = Q[80:144] K^T (M=64)   (N=144, K=64, K-major)
+//                  O  = P[0:128]  V   (M=128), O2 = P[80:144] V   (M=64)   (N=64, K=144, V MN-major)
 //                in whatever order their inputs become ready (non-blocking barrier tests),
 //                signalling completion with tcgen05.commit on mbarriers.
 //   warps 4..11  softmax + epilogue of rows 0..127: two warpgroups split every row, 72 key columns
@@ -420,7 +422,7 @@ attn_sync_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
 //                memory. S comes from TMEM (32x32b loads, one lane = one row per thread), P goes to
 //                shared memory as bf16 in the UMMA A-operand layout, O rows are scaled by 1/sum and
 //                written to global memory as bf16.
-//   warp 3       rows 128..143 from S2/O2 TMEM lanes 112..127 with 16x256b loads (16 rows spread
+//   warp 3       rows 128..143 from S2/O2 TMEM lanes 96..111 / 112..127 with 16x256b loads (16 rows spread
 //                over the 32 threads, two rows per thread, reductions over 4-thread quads).
 // The shifted-window mask is turned into a bit per key once per window and reused by its heads; a
 // window with a single region skips masking. Every wait is bounded (status word + abort flag).
@@ -428,21 +430,28 @@ attn_sync_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
 namespace tc {
 
 constexpr int kStages = 3;
-constexpr int kStageBytes = 3 * kTileBytes;  // Q, K, V (bf16, 144 x 128 B each)
+constexpr int kQKBytes = 2 * kTileBytes;  // Q and K of a tile (bf16, 144 x 128 B each)
+constexpr int kVBytes = kTileBytes;       // V of a tile
+constexpr int kStageBytes = kQKBytes + kVBytes;
 constexpr int kPChunk = kTileBytes;          // 64 keys x 144 rows of bf16
 constexpr int kPBytes = 3 * kPChunk;         // keys 0-63, 64-127, 128-143 (+ unused tail)
 constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // {max, sum} x warpgroup x row
 constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColS2 = 160, kColO0 = 320, kColO1 = 384, kColO2 = 448;
-constexpr int kNumBars = 20;
+constexpr int kNumBars = 28;
 constexpr int kSmem = kStages * kStageBytes + kPBytes + kXchgBytes + kNumBars * 8 + 16 + 1024;
 constexpr uint32_t kIdescS = ptx::make_idesc(1, 128, kMaxN, false, false);
 constexpr uint32_t kIdescO = ptx::make_idesc(1, 128, 64, false, true);
-constexpr uint32_t kRowOff16 = 16 * 128;  // 16 rows of a 128-byte-row tile (swizzle-atom aligned)
+// Rows 128..143 go through M=64 UMMAs over rows 80..143: A rows 48..63 land in TMEM lanes 96..111
+// (lane offset 0) or 112..127 (lane offset 16), so two M=64 accumulators share the same columns.
+constexpr uint32_t kIdescS2 = ptx::make_idesc(1, 64, kMaxN, false, false);
+constexpr uint32_t kIdescO2 = ptx::make_idesc(1, 64, 64, false, true);
+constexpr uint32_t kRowOff80 = 80 * 128;  // 80 rows of a 128-byte-row tile (swizzle-atom aligned)
+constexpr uint32_t kLaneHalf = 16u << 16;
 
-enum { kFull = 0, kEmpty = 3, kSFull = 6, kSFree = 7, kPFull = 8, kPEmpty = 9, kOFull = 10, kOFree = 12,
-       kO2Full = 14, kO2Free = 15, kDone = 16, kXMax = 17, kXSum = 18 };
+enum { kFullQK = 0, kEmptyQK = 3, kFullV = 6, kEmptyV = 9, kSFull = 12, kSFree = 13, kPFull = 14, kPEmpty = 15,
+       kOFull = 16, kOFree = 18, kO2Full = 20, kO2Free = 22, kDone = 24, kXMax = 25, kXSum = 26 };
 
 __device__ __forceinline__ uint32_t nibble_of_bytes(uint32_t ne) {
   return (ne & 1u) | ((ne >> 7) & 2u) | ((ne >> 14) & 4u) | ((ne >> 21) & 8u);
@@ -550,8 +559,10 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
   if (threadIdx.x == 0) {
     abort_flag = 0;
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(BAR(kFull + s), 1);
-      mbar_init(BAR(kEmpty + s), 1);
+      mbar_init(BAR(kFullQK + s), 1);
+      mbar_init(BAR(kEmptyQK + s), 1);
+      mbar_init(BAR(kFullV + s), 1);
+      mbar_init(BAR(kEmptyV + s), 1);
     }
     mbar_init(BAR(kSFull), 1);
     mbar_init(BAR(kSFree), 9);  // 8 softmax warps + the rows-128..143 warp
@@ -561,8 +572,10 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       mbar_init(BAR(kOFull + b), 1);
       mbar_init(BAR(kOFree + b), 8);
     }
-    mbar_init(BAR(kO2Full), 1);
-    mbar_init(BAR(kO2Free), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(BAR(kO2Full + b), 1);
+      mbar_init(BAR(kO2Free + b), 1);
+    }
     mbar_init(BAR(kDone), 1);
     mbar_init(BAR(kXMax), 8);  // row-max exchange between the two softmax warpgroups
     mbar_init(BAR(kXSum), 8);  // row-sum exchange
@@ -580,29 +593,40 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
   const bool full_n = p.N == kMaxN;
   const float braw = kMaskedLog2 / p.scale_log2;  // -100 / scale: the mask bias before scaling
 
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
+  if (warp == 0 || warp == 2) {
+    // ---------------- TMA producers: warp 0 loads Q and K, warp 2 loads V ----------------
+    // Q/K slots are released as soon as the S UMMAs of their tile complete, V slots after PV, so
+    // the Q/K loads of later tiles do not wait for the PV of earlier ones.
     if (lane == 0) {
-      tma_prefetch_desc(&tmq);
-      tma_prefetch_desc(&tmk);
-      tma_prefetch_desc(&tmv);
+      const bool qk = warp == 0;
+      const int full0 = qk ? kFullQK : kFullV, empty0 = qk ? kEmptyQK : kEmptyV;
+      const uint32_t bytes = qk ? (uint32_t)kQKBytes : (uint32_t)kVBytes;
+      if (qk) {
+        tma_prefetch_desc(&tmq);
+        tma_prefetch_desc(&tmk);
+      } else {
+        tma_prefetch_desc(&tmv);
+      }
       int last_par[kStages] = {-1, -1, -1};
       for (int i = 0; i < n_local; ++i) {
         const int t = t_begin + i;
         const int s = i % kStages;
         const uint32_t ph = (uint32_t)((i / kStages) & 1);
-        if (!mbar_wait(BAR(kEmpty + s), ph ^ 1u, abort, p.status, 11, kTimeoutNs)) break;
+        if (!mbar_wait(BAR(empty0 + s), ph ^ 1u, abort, p.status, 11, kTimeoutNs)) break;
         const int w = t / p.H, h = t - w * p.H;
-        const uint32_t dst = sbase + s * kStageBytes;
-        mbar_arrive_expect_tx(BAR(kFull + s), kStageBytes);
-        tma_load_4d(dst, &tmq, BAR(kFull + s), 0, 0, h, w);
-        tma_load_4d(dst + kTileBytes, &tmk, BAR(kFull + s), 0, 0, h, w);
-        tma_load_4d(dst + 2 * kTileBytes, &tmv, BAR(kFull + s), 0, 0, h, w);
+        const uint32_t dst = sbase + s * kStageBytes + (qk ? 0u : (uint32_t)kQKBytes);
+        mbar_arrive_expect_tx(BAR(full0 + s), bytes);
+        if (qk) {
+          tma_load_4d(dst, &tmq, BAR(full0 + s), 0, 0, h, w);
+          tma_load_4d(dst + kTileBytes, &tmk, BAR(full0 + s), 0, 0, h, w);
+        } else {
+          tma_load_4d(dst, &tmv, BAR(full0 + s), 0, 0, h, w);
+        }
         last_par[s] = (int)ph;
       }
       int no_abort = 0;
       for (int s = 0; s < kStages; ++s)
-        if (last_par[s] >= 0) mbar_wait(BAR(kFull + s), (uint32_t)last_par[s], &no_abort, p.status, 12, kTimeoutNs);
+        if (last_par[s] >= 0) mbar_wait(BAR(full0 + s), (uint32_t)last_par[s], &no_abort, p.status, 12, kTimeoutNs);
     }
   } else if (warp == 1) {
     // ---------------- UMMA issuer (event loop) ----------------
@@ -614,7 +638,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
         bool progressed = false;
         if (ns < n_local) {
           const int s = ns % kStages;
-          if (mbar_test_wait(BAR(kFull + s), (uint32_t)((ns / kStages) & 1)) &&
+          if (mbar_test_wait(BAR(kFullQK + s), (uint32_t)((ns / kStages) & 1)) &&
               mbar_test_wait(BAR(kSFree), (uint32_t)((ns & 1) ^ 1))) {
             tc_fence_after();
             const uint32_t sQ = sbase + s * kStageBytes, sK = sQ + kTileBytes;
@@ -622,9 +646,10 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
             for (int k = 0; k < 4; ++k) {
               const uint64_t b = desc_sw128(sK + k * 32, 16, 1024);
               umma_f16(tmem + kColS, desc_sw128(sQ + k * 32, 16, 1024), b, kIdescS, k > 0 ? 1u : 0u);
-              umma_f16(tmem + kColS2, desc_sw128(sQ + kRowOff16 + k * 32, 16, 1024), b, kIdescS, k > 0 ? 1u : 0u);
+              umma_f16(tmem + kColS2, desc_sw128(sQ + kRowOff80 + k * 32, 16, 1024), b, kIdescS2, k > 0 ? 1u : 0u);
             }
             umma_commit(BAR(kSFull));
+            umma_commit(BAR(kEmptyQK + s));
             ++ns;
             progressed = true;
           }
@@ -632,22 +657,24 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
         if (npv < ns) {
           const int j = npv, s = j % kStages, ob = j & 1;
           if (mbar_test_wait(BAR(kPFull), (uint32_t)(j & 1)) &&
+              mbar_test_wait(BAR(kFullV + s), (uint32_t)((j / kStages) & 1)) &&
               mbar_test_wait(BAR(kOFree + ob), (uint32_t)(((j >> 1) & 1) ^ 1)) &&
-              mbar_test_wait(BAR(kO2Free), (uint32_t)((j & 1) ^ 1))) {
+              mbar_test_wait(BAR(kO2Free + ob), (uint32_t)(((j >> 1) & 1) ^ 1))) {
             tc_fence_after();
-            const uint32_t sV = sbase + s * kStageBytes + 2 * kTileBytes;
+            const uint32_t sV = sbase + s * kStageBytes + kQKBytes;
             const uint32_t dO = tmem + (ob ? kColO1 : kColO0);
+            const uint32_t dO2 = tmem + kColO2 + (ob ? kLaneHalf : 0u);
 #pragma unroll
             for (int k = 0; k < 9; ++k) {
               const uint32_t pa = sP + (k >> 2) * kPChunk + (k & 3) * 32;
               const uint64_t b = desc_sw128(sV + k * 2048, kTileBytes, 1024);
               umma_f16(dO, desc_sw128(pa, 16, 1024), b, kIdescO, k > 0 ? 1u : 0u);
-              umma_f16(tmem + kColO2, desc_sw128(pa + kRowOff16, 16, 1024), b, kIdescO, k > 0 ? 1u : 0u);
+              umma_f16(dO2, desc_sw128(pa + kRowOff80, 16, 1024), b, kIdescO2, k > 0 ? 1u : 0u);
             }
             umma_commit(BAR(kOFull + ob));
-            umma_commit(BAR(kO2Full));
+            umma_commit(BAR(kO2Full + ob));
             umma_commit(BAR(kPEmpty));
-            umma_commit(BAR(kEmpty + s));
+            umma_commit(BAR(kEmptyV + s));
             ++npv;
             progressed = true;
           }
@@ -785,7 +812,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
     // ---------------- rows 128..143 (S2/O2 lanes 112..127, 16x256b) ----------------
     const int t0 = lane & 3, t1 = lane >> 2;
     const int ra = 128 + t1, rb = 136 + t1;
-    const uint32_t lane_addr = 112u << 16;
+    const uint32_t lane_addr = 96u << 16;  // A rows 48..63 of the M=64 blocks
     int cached_w = -1;
     uint32_t ta = 0, tb = 0, kp[18];
     bool wmask = false;
@@ -795,14 +822,15 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
     int t_prev = -1, j_prev = -1;
 
     auto epilogue_rem = [&](int j, int t, float la, float lb) -> bool {
-      if (!mbar_wait(BAR(kO2Full), (uint32_t)(j & 1), abort, p.status, 23, kTimeoutNs)) return false;
+      const int ob = j & 1;
+      if (!mbar_wait(BAR(kO2Full + ob), (uint32_t)((j >> 1) & 1), abort, p.status, 23, kTimeoutNs)) return false;
       tc_fence_after();
       uint32_t o[32];
-      tmem_ld_16x256b_r32(tmem + lane_addr + kColO2, o);
+      tmem_ld_16x256b_r32(tmem + lane_addr + kColO2 + (ob ? kLaneHalf : 0u), o);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kO2Free));
+      if (lane == 0) mbar_arrive(BAR(kO2Free + ob));
       const int w = t / p.H, h = t - w * p.H;
       __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)w * p.os_w + (int64_t)h * p.os_h;
       const float ia = 1.f / la, ib = 1.f / lb;
@@ -865,10 +893,6 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kSFree));
-      if (j_prev >= 0) {  // O2 is single-buffered: drain it before the next PV can start
-        if (!epilogue_rem(j_prev, t_prev, la_prev, lb_prev)) { ok = false; break; }
-        j_prev = -1;
-      }
       // v[4j + {0,1}] = row ra, keys 8j + 2t0 + {0,1}; v[4j + {2,3}] = row rb, same keys.
       float mxa = -INFINITY, mxb = -INFINITY;
 #pragma unroll
@@ -930,6 +954,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kPFull));
+      if (j_prev >= 0 && !epilogue_rem(j_prev, t_prev, la_prev, lb_prev)) { ok = false; break; }
       j_prev = i;
       t_prev = t;
       la_prev = la;
