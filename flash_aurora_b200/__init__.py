@@ -19,14 +19,19 @@ from .adaln import (
     adaptive_layernorm_film_add_residual_forward,
     adaptive_layernorm_film_forward,
     unmerge_adaptive_layernorm_film_add_residual,
+    unmerge_adaptive_layernorm_film_add_residual_band,
 )
+from .sharding import BandContext, HaloExchangeError, band_bounds
 from .swin3d_layout import (
+    band_halo_extract,
     crop_roll_unmerge_windows,
+    crop_roll_unmerge_windows_band,
     crop_roll_unmerge_windows_triton,
     roll_pad_partition_windows,
+    roll_pad_partition_windows_band,
     roll_pad_partition_windows_triton,
 )
-from .util import maybe_adjust_windows, window_geometry
+from .util import band_geometry, maybe_adjust_windows, window_geometry
 from .window_attn import (
     WinAttnPrecision,
     shifted_window_group_ids,
@@ -40,6 +45,14 @@ __all__ = [
     "adaptive_layernorm_film_add_residual_forward",
     "adaptive_layernorm_film_forward",
     "unmerge_adaptive_layernorm_film_add_residual",
+    "unmerge_adaptive_layernorm_film_add_residual_band",
+    "BandContext",
+    "HaloExchangeError",
+    "band_bounds",
+    "band_geometry",
+    "band_halo_extract",
+    "crop_roll_unmerge_windows_band",
+    "roll_pad_partition_windows_band",
     "crop_roll_unmerge_windows",
     "crop_roll_unmerge_windows_triton",
     "roll_pad_partition_windows",

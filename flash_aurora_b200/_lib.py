@@ -36,6 +36,13 @@ SIGNATURES = {
     "fa_adaln_film": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _f32, _f32, _vp, _i32, _vp, _i64, _i64, _i64, _vp]),
     "fa_unmerge_adaln_film": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _f32, _f32, _vp, _i32, _vp,
                                      _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
+    "fa_roll_pad_partition_band": (_i32, [_vp, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64,
+                                          _i32p, _i32p, _vp]),
+    "fa_band_halo_extract": (_i32, [_vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
+    "fa_crop_roll_unmerge_band": (_i32, [_vp, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64,
+                                         _i32p, _i32p, _vp]),
+    "fa_unmerge_adaln_film_band": (_i32, [_vp, _vp, _i32, _vp, _i32, _vp, _vp, _i32, _f32, _f32, _vp, _i32, _vp,
+                                          _i64, _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
     "fa_shifted_window_groups": (_i32, [_i64, _i64, _i64, _i32p, _i32p, _i32, _u8p]),
     "fa_window_attention": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64p, _u8p, _u8p, _i64, _f32, _vp]),
     "fa_window_attention_qkvpacked": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _u8p, _u8p, _i64, _f32, _vp]),

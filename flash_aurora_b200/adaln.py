@@ -14,12 +14,13 @@ from typing import Optional
 import torch
 
 from . import _lib
-from .util import window_geometry
+from .util import band_geometry, window_geometry
 
 __all__ = [
     "adaptive_layernorm_film_forward",
     "adaptive_layernorm_film_add_residual_forward",
     "unmerge_adaptive_layernorm_film_add_residual",
+    "unmerge_adaptive_layernorm_film_add_residual_band",
 ]
 
 _MAX_D = 2048
@@ -32,6 +33,14 @@ def _mod_rows(t: torch.Tensor, B: int, D: int, name: str) -> torch.Tensor:
     if t.dtype not in _DTYPES:
         raise ValueError(f"{name} must be float32 or bfloat16")
     return t.reshape(B, D).contiguous()
+
+
+def _check_out_bf16(out_bf16: Optional[torch.Tensor], B: int, L: int, D: int, device) -> None:
+    if out_bf16 is None:
+        return
+    if (tuple(out_bf16.shape) != (B, L, D) or out_bf16.dtype != torch.bfloat16
+            or not out_bf16.is_contiguous() or out_bf16.device != device):
+        raise ValueError(f"out_bf16 must be a contiguous bfloat16 tensor of shape {(B, L, D)} on {device}")
 
 
 def _launch(x, residual, scale, shift, scale_bias, eps, out, out_bf16, B, L, D, what):
@@ -99,6 +108,10 @@ def adaptive_layernorm_film_add_residual_forward(
     out_dtype = torch.float32 if output_fp32 else x.dtype
     if out is None:
         out = torch.empty(B, L, D, device=x.device, dtype=out_dtype)
+    elif (tuple(out.shape) != (B, L, D) or out.dtype != out_dtype or not out.is_contiguous()
+          or out.device != x.device):
+        raise ValueError(f"out must be a contiguous {out_dtype} tensor of shape {(B, L, D)} on {x.device}")
+    _check_out_bf16(out_bf16, B, L, D, x.device)
     _launch(x.contiguous(), residual.contiguous(), scale, shift, scale_bias, eps, out, out_bf16, B, L, D,
             "adaptive_layernorm_film_add_residual_forward")
     return out
@@ -135,6 +148,7 @@ def unmerge_adaptive_layernorm_film_add_residual(
     _, _, _, _, nW, N = window_geometry(tuple(res), tuple(window_size), tuple(shift_size))
     if tuple(windows.shape) != (B * nW, N, D):
         raise ValueError(f"windows must have shape {(B * nW, N, D)}, got {tuple(windows.shape)}")
+    _check_out_bf16(out_bf16, B, L, D, residual.device)
     scale = _mod_rows(scale, B, D, "scale")
     shift = _mod_rows(shift, B, D, "shift").to(scale.dtype)
     out = torch.empty(B, L, D, device=residual.device, dtype=torch.float32)
@@ -144,4 +158,59 @@ def unmerge_adaptive_layernorm_film_add_residual(
         float(eps), out.data_ptr(), _lib.FA_F32, out_bf16.data_ptr() if out_bf16 is not None else None,
         B, C, H, W, D, _lib.i32x3(window_size), _lib.i32x3(shift_size), _lib.stream_ptr(residual.device))
     _lib.check(rc, "unmerge_adaptive_layernorm_film_add_residual")
+    return out
+
+
+def unmerge_adaptive_layernorm_film_add_residual_band(
+    windows: torch.Tensor,
+    halo_in: Optional[torch.Tensor],
+    residual: torch.Tensor,
+    scale: torch.Tensor,
+    shift: torch.Tensor,
+    band_res: tuple[int, int, int],
+    field_res: tuple[int, int, int],
+    window_size: tuple[int, int, int],
+    shift_size: tuple[int, int, int],
+    scale_bias: float = 0.0,
+    eps: float = 1e-5,
+    *,
+    out_bf16: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Latitude-band form of :func:`unmerge_adaptive_layernorm_film_add_residual`: the band's first
+    ``s = shift_h`` rows are read from ``halo_in (B, C, s, W, D)``, the previous band's halo
+    extract (same dtype as ``windows``)."""
+    _lib.require_cuda(windows, "unmerge_adaptive_layernorm_film_add_residual_band")
+    _lib.require_cuda(residual, "unmerge_adaptive_layernorm_film_add_residual_band")
+    if windows.dtype not in _DTYPES or residual.dtype != torch.float32:
+        raise ValueError("windows must be float32/bfloat16 and residual float32")
+    C, Hb, W = (int(v) for v in band_res)
+    B, L, D = residual.shape
+    if L != C * Hb * W:
+        raise ValueError(f"residual has {L} tokens, band {tuple(band_res)} has {C * Hb * W}")
+    if D > _MAX_D:
+        raise ValueError(f"AdaLN supports D <= {_MAX_D}")
+    ws, ss, nW, N = band_geometry(band_res, field_res, window_size, shift_size)
+    if tuple(windows.shape) != (B * nW, N, D):
+        raise ValueError(f"windows must have shape {(B * nW, N, D)}, got {tuple(windows.shape)}")
+    if ss[1]:
+        if halo_in is None:
+            raise ValueError(f"a band with an H shift of {ss[1]} rows needs halo_in")
+        if tuple(halo_in.shape) != (B, C, ss[1], W, D) or halo_in.dtype != windows.dtype:
+            raise ValueError(f"halo_in must be {windows.dtype} of shape {(B, C, ss[1], W, D)}")
+        _lib.require_cuda(halo_in, "unmerge_adaptive_layernorm_film_add_residual_band")
+        halo_in = halo_in.contiguous()
+    else:
+        halo_in = None
+    _check_out_bf16(out_bf16, B, L, D, residual.device)
+    scale = _mod_rows(scale, B, D, "scale")
+    shift = _mod_rows(shift, B, D, "shift").to(scale.dtype)
+    windows, residual = windows.contiguous(), residual.contiguous()
+    out = torch.empty(B, L, D, device=residual.device, dtype=torch.float32)
+    rc = _lib.load().fa_unmerge_adaln_film_band(
+        windows.data_ptr(), halo_in.data_ptr() if halo_in is not None else None, _lib.dtype_code(windows.dtype),
+        residual.data_ptr(), _lib.FA_F32, scale.data_ptr(), shift.data_ptr(), _lib.dtype_code(scale.dtype),
+        float(scale_bias), float(eps), out.data_ptr(), _lib.FA_F32,
+        out_bf16.data_ptr() if out_bf16 is not None else None, B, C, Hb, field_res[1], W, D,
+        _lib.i32x3(window_size), _lib.i32x3(shift_size), _lib.stream_ptr(residual.device))
+    _lib.check(rc, "unmerge_adaptive_layernorm_film_add_residual_band")
     return out

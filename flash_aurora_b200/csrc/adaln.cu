@@ -50,6 +50,7 @@ struct AdaArgs {
   int32_t D;
   bool gather;
   LayoutParams lp;
+  const void* halo_in;  // band mode: halo-back rows of the first lp.band band rows (x dtype)
 };
 
 // kChunks = number of 8-element (vector path) or 1-element (scalar path) chunks per lane.
@@ -59,7 +60,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) adaln_kernel(AdaArgs a) {
   const int lane = threadIdx.x & 31;
   const int D = a.D;
   const int64_t rows = a.B * a.L;
-  const TX* __restrict__ xg = reinterpret_cast<const TX*>(a.x);
+  const TX* const xwin = reinterpret_cast<const TX*>(a.x);
   const TO* __restrict__ rg = reinterpret_cast<const TO*>(a.residual);
   TO* __restrict__ og = reinterpret_cast<TO*>(a.out);
   const float inv_d = 1.0f / (float)D;
@@ -68,12 +69,20 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) adaln_kernel(AdaArgs a) {
        row += (int64_t)gridDim.x * kWarpsPerBlock) {
     const int64_t b = row / a.L;
     int64_t xrow = row;
+    const TX* xg = xwin;
     if (a.gather) {
       const int32_t t = (int32_t)(row - b * a.L);
       const int32_t w = t % a.lp.W;
-      const int32_t h = (t / a.lp.W) % a.lp.H;
-      const int32_t c = t / (a.lp.W * a.lp.H);
-      xrow = b * (int64_t)a.lp.nW * a.lp.N + unmerge_slot(a.lp, c, h, w);
+      const int32_t h = (t / a.lp.W) % a.lp.Hout;
+      const int32_t c = t / (a.lp.W * a.lp.Hout);
+      const int32_t slot = unmerge_slot(a.lp, c, h, w);
+      if (slot >= 0) {
+        xrow = b * (int64_t)a.lp.nW * a.lp.N + slot;
+      } else {
+        // Band mode: row computed by the previous band, received into the halo-back buffer.
+        xg = reinterpret_cast<const TX*>(a.halo_in);
+        xrow = b * (int64_t)a.lp.C * a.lp.band * a.lp.W + (-1 - slot);
+      }
     }
     const TX* xr = xg + xrow * D;
     float v[kChunks][kE];
@@ -177,7 +186,7 @@ int run_adaln(AdaArgs a, int x_dtype, int residual_dtype, int mod_dtype, int out
   a.mod_bf16 = mod_dtype == FA_BF16;
   const bool vec = (a.D % 8 == 0) && aligned16(a.x) && aligned16(a.scale) && aligned16(a.shift) &&
                    aligned16(a.out) && (!a.residual || aligned16(a.residual)) &&
-                   (!a.out_bf16 || aligned16(a.out_bf16));
+                   (!a.out_bf16 || aligned16(a.out_bf16)) && (!a.halo_in || aligned16(a.halo_in));
   if (x_dtype == FA_F32) return launch_adaln<float, float>(a, vec, s);
   if (out_dtype == FA_F32) return launch_adaln<__nv_bfloat16, float>(a, vec, s);
   return launch_adaln<__nv_bfloat16, __nv_bfloat16>(a, vec, s);
@@ -216,5 +225,29 @@ extern "C" int fa_unmerge_adaln_film(const void* windows, int windows_dtype, con
   a.scale_bias = scale_bias; a.eps = eps; a.out = out;
   a.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);
   a.B = B; a.L = C * H * W; a.D = (int32_t)D; a.gather = true; a.lp = layout_params(g);
+  return run_adaln(a, windows_dtype, residual_dtype, mod_dtype, out_dtype, (cudaStream_t)stream);
+}
+
+extern "C" int fa_unmerge_adaln_film_band(const void* windows, const void* halo_in,
+                                          int windows_dtype, const void* residual,
+                                          int residual_dtype, const void* scale, const void* shift,
+                                          int mod_dtype, float scale_bias, float eps, void* out,
+                                          int out_dtype, void* out_bf16, int64_t B, int64_t C,
+                                          int64_t H_band, int64_t H_field, int64_t W, int64_t D,
+                                          const int32_t window_size[3],
+                                          const int32_t shift_size[3], void* stream) {
+  Geometry g;
+  int rc = make_band_geometry(C, H_band, H_field, W, window_size, shift_size, &g);
+  if (rc != FA_OK) return rc;
+  FA_REQUIRE(D < (1 << 30), FA_ERR_INVALID, "D too large");
+  AdaArgs a{};
+  a.x = windows; a.residual = residual; a.scale = scale; a.shift = shift;
+  a.scale_bias = scale_bias; a.eps = eps; a.out = out;
+  a.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);
+  a.B = B; a.L = C * H_band * W; a.D = (int32_t)D; a.gather = true;
+  a.lp = band_layout_params(g, false);
+  a.halo_in = halo_in;
+  FA_REQUIRE(halo_in || a.lp.band == 0 || B == 0 || D == 0, FA_ERR_INVALID,
+             "shifted band needs the halo-back rows");
   return run_adaln(a, windows_dtype, residual_dtype, mod_dtype, out_dtype, (cudaStream_t)stream);
 }

@@ -70,6 +70,23 @@ int make_geometry(int64_t C, int64_t H, int64_t W, const int32_t* window_size,
   return FA_OK;
 }
 
+int make_band_geometry(int64_t C, int64_t H_band, int64_t H_field, int64_t W,
+                       const int32_t* window_size, const int32_t* shift_size, Geometry* g) {
+  int rc = make_geometry(C, H_field, W, window_size, shift_size, g);
+  if (rc != FA_OK) return rc;
+  const int32_t wh = g->ws[1];
+  FA_REQUIRE(g->padded[1] == H_field, FA_ERR_UNSUPPORTED,
+             "band sharding needs the field height to be a multiple of the window height");
+  FA_REQUIRE(H_band > 0 && H_band <= H_field && H_band % wh == 0, FA_ERR_INVALID,
+             "band height must be a positive multiple of the window height, at most the field height");
+  FA_REQUIRE(g->ss[1] <= H_band, FA_ERR_INVALID, "halo deeper than the band");
+  g->H = H_band;
+  g->padded[1] = H_band;
+  g->grid[1] = H_band / wh;
+  g->nW = g->grid[0] * g->grid[1] * g->grid[2];
+  return FA_OK;
+}
+
 }  // namespace fa
 
 using namespace fa;

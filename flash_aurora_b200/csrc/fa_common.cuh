@@ -44,6 +44,12 @@ struct Geometry {
 int make_geometry(int64_t C, int64_t H, int64_t W, const int32_t* window_size,
                   const int32_t* shift_size, Geometry* g);
 
+// Geometry of one latitude band of H_band rows out of a field of H_field rows: window clamping
+// and shifts are decided on the whole field (C, H_field, W); the band must hold whole window
+// rows, and the field must need no H padding.
+int make_band_geometry(int64_t C, int64_t H_band, int64_t H_field, int64_t W,
+                       const int32_t* window_size, const int32_t* shift_size, Geometry* g);
+
 // Device-side copy of the index parameters of a layout gather.
 struct LayoutParams {
   int32_t C, H, W;
@@ -52,6 +58,13 @@ struct LayoutParams {
   int32_t pc, ph, pw;  // front pads
   int32_t W1, HW1;     // windows along W, windows per C slab
   int32_t nW, N;
+  // Latitude-band mode (band > 0): the grid is one band of H rows of a larger field and the
+  // cyclic H shift is realised by the band offset instead of a wrap. Shifted row s of the band
+  // is original band row s + band; rows at or past H come from a halo of `band` rows (the next
+  // band's first rows, layout (B, C, band, W, D)). sh is 0 in band mode.
+  int32_t band;
+  int32_t Hout;  // rows of an unmerge output grid: H, or `band` for the halo extract
+  int32_t hs0;   // band mode: shifted row of unmerge output row 0 (-band, or H - band)
 };
 
 inline LayoutParams layout_params(const Geometry& g) {
@@ -64,11 +77,27 @@ inline LayoutParams layout_params(const Geometry& g) {
   p.HW1 = (int32_t)(g.grid[1] * g.grid[2]);
   p.nW = (int32_t)g.nW;
   p.N = g.N;
+  p.band = 0;
+  p.Hout = p.H;
+  p.hs0 = 0;
+  return p;
+}
+
+// Band-mode parameters: `g` is the geometry of the band (H = band rows, shifts as for the whole
+// field); the H shift becomes the halo depth. `extract` selects the halo-extract unmerge grid
+// (the band's last `band` shifted rows, which are the next band's first original rows).
+inline LayoutParams band_layout_params(const Geometry& g, bool extract) {
+  LayoutParams p = layout_params(g);
+  p.band = p.sh;
+  p.sh = 0;
+  p.Hout = extract ? p.band : p.H;
+  p.hs0 = extract ? p.H - p.band : -p.band;
   return p;
 }
 
 // Source token (c*H + h)*W + w of window slot (win, n) of one batch element, or -1 for pad.
-// Same mapping as ops/triton_swin3d_layout.py:218-246.
+// Same mapping as ops/triton_swin3d_layout.py:218-246. In band mode a result >= C*H*W is
+// halo token (result - C*H*W) of layout (C, band, W).
 __device__ __forceinline__ int32_t partition_source(const LayoutParams& p, int32_t win, int32_t n) {
   const int32_t c1 = win / p.HW1;
   const int32_t r1 = win - c1 * p.HW1;
@@ -84,15 +113,32 @@ __device__ __forceinline__ int32_t partition_source(const LayoutParams& p, int32
   const int32_t wsv = w1 * p.ww + ww - p.pw;
   if (cs < 0 || cs >= p.C || hs < 0 || hs >= p.H || wsv < 0 || wsv >= p.W) return -1;
   int32_t xc = cs + p.sc; if (xc >= p.C) xc -= p.C;
-  int32_t xh = hs + p.sh; if (xh >= p.H) xh -= p.H;
   int32_t xw = wsv + p.sw; if (xw >= p.W) xw -= p.W;
+  int32_t xh = hs + p.sh + p.band;
+  if (xh >= p.H) {
+    if (p.band == 0) {
+      xh -= p.H;
+    } else {
+      // Band mode: rows past the band are halo rows, encoded after the band's C*H*W tokens.
+      return p.C * p.H * p.W + (xc * p.band + (xh - p.H)) * p.W + xw;
+    }
+  }
   return (xc * p.H + xh) * p.W + xw;
 }
 
 // Window slot win*N + n holding token (c, h, w) of one batch element (triton_swin3d_layout.py:283-305).
+// (c, h, w) indexes the unmerge output grid (C, Hout, W). In band mode a negative result
+// -1 - i means halo-back token i.
 __device__ __forceinline__ int32_t unmerge_slot(const LayoutParams& p, int32_t c, int32_t h, int32_t w) {
   int32_t cs = c - p.sc; if (cs < 0) cs += p.C;
-  int32_t hs = h - p.sh; if (hs < 0) hs += p.H;
+  int32_t hs = h - p.sh + p.hs0;
+  if (p.band == 0) {
+    if (hs < 0) hs += p.H;
+  } else if (hs < 0) {
+    // Band mode: the first `band` original rows were computed by the previous band; they are
+    // read from its halo-back buffer (layout (C, band, W)), encoded as -1 - index.
+    return -1 - ((c * p.band + h) * p.W + w);
+  }
   int32_t wsv = w - p.sw; if (wsv < 0) wsv += p.W;
   const int32_t pc = cs + p.pc, ph = hs + p.ph, pw = wsv + p.pw;
   const int32_t c1 = pc / p.wc, wc = pc - c1 * p.wc;

@@ -1,0 +1,243 @@
+"""Latitude-band sharding of a Swin3D field across ranks (one process per GPU).
+
+The upstream backbone runs one field per device; its only multi-device path places whole
+stages on different GPUs (engine/distributed/rollout_pipeline.py:137-169) and never splits a
+field. Here a field ``(C, H, W)`` is split along H into bands of whole window rows, one band per
+rank:
+
+* windows are independent given their tokens and MLP/AdaLN are per token, so an unshifted block
+  is fully local;
+* a shifted block (H shift ``s = ws_h // 2``, swin3d.py:999-1001) rolls the field by ``-s`` rows
+  (swin3d.py:757-770): the band's shifted windows start ``s`` rows into the band and end ``s``
+  rows into the next band. Each rank therefore receives the next band's first ``s`` rows (the
+  forward halo) before the partition, and after the attention it sends the outputs of its last
+  ``s`` shifted rows back to their owner (the halo-back rows), which reads them in the fused
+  unmerge + AdaLN. The last band wraps to band 0, exactly like ``torch.roll``.
+
+Those two NCCL point-to-point exchanges per shifted block are the only collectives; there is no
+remote TMA and no multicast. The shifted-window mask depends on the global window position, so a
+band's region ids are the rows ``[h1_begin, h1_end)`` of the field's ``(nW, N)`` ids.
+
+``exchange`` works for any backend: NCCL tensors on the GPU (the product path) and gloo CPU
+tensors (the multi-process tests). Waits are bounded by ``timeout_s``: a peer that never sends
+surfaces as :class:`HaloExchangeError` on the host, never as a hang.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from datetime import timedelta
+from typing import Callable, Optional
+
+import torch
+
+from .util import maybe_adjust_windows
+
+__all__ = [
+    "HaloExchangeError",
+    "band_bounds",
+    "BandContext",
+    "LocalRing",
+]
+
+
+class HaloExchangeError(RuntimeError):
+    """A halo exchange with a neighbouring band did not complete."""
+
+
+def band_bounds(field_res, window_size, world: int) -> list[tuple[int, int]]:
+    """Token-row range ``[h_begin, h_end)`` of each rank's band.
+
+    The field's window rows ``H // wh`` are split as evenly as possible (the first bands get the
+    smaller share), so bands differ by at most one window row. Requires ``H % wh == 0`` and at
+    least one window row per rank.
+    """
+    C, H, W = (int(v) for v in field_res)
+    ws, _ = maybe_adjust_windows(tuple(window_size), (0, 0, 0), (C, H, W))
+    wh = ws[1]
+    if H % wh != 0:
+        raise ValueError(f"band sharding needs H ({H}) to be a multiple of the window height ({wh})")
+    rows = H // wh
+    if world < 1 or world > rows:
+        raise ValueError(f"cannot split {rows} window rows across {world} ranks")
+    cuts = [(r * rows) // world for r in range(world + 1)]
+    return [(cuts[r] * wh, cuts[r + 1] * wh) for r in range(world)]
+
+
+@dataclass
+class LocalRing:
+    """In-process stand-in for the ranks of a ring: ``world`` threads of one process exchange
+    tensors through shared slots. Used to run several bands on one device (tests, and the
+    single-process check of the sharded block); every participant must call ``exchange`` the
+    same number of times, as with a real process group."""
+
+    world: int
+    timeout_s: float = 60.0
+    _slots: dict = field(default_factory=dict)
+
+    def __post_init__(self) -> None:
+        import threading
+
+        self._barrier = threading.Barrier(self.world, timeout=self.timeout_s)
+
+    def exchange(self, rank: int, send: torch.Tensor, recv: torch.Tensor, dst: int, src: int) -> None:
+        import threading
+
+        try:
+            self._slots[(rank, dst)] = send
+            self._barrier.wait()
+            recv.copy_(self._slots[(src, rank)])
+            self._barrier.wait()
+        except threading.BrokenBarrierError as e:
+            raise HaloExchangeError(f"rank {rank}: local ring exchange with rank {src} timed out") from e
+        finally:
+            self._slots.pop((rank, dst), None)
+
+
+class BandContext:
+    """One rank's band of a field plus the halo exchanges with its neighbours.
+
+    ``group``: a ``torch.distributed`` process group (default: the world group) when the ranks
+    are processes; ``ring``: a :class:`LocalRing` when they are threads of one process; neither
+    when ``world == 1`` (the band is the whole field and the halo wraps onto itself).
+    """
+
+    def __init__(self, field_res, window_size, rank: int, world: int, *, group=None,
+                 ring: Optional[LocalRing] = None, timeout_s: float = 60.0) -> None:
+        self.field_res = tuple(int(v) for v in field_res)
+        self.window_size = tuple(int(v) for v in window_size)
+        self.rank, self.world = int(rank), int(world)
+        if not 0 <= self.rank < self.world:
+            raise ValueError(f"rank {rank} outside world {world}")
+        self.bounds = band_bounds(self.field_res, self.window_size, self.world)
+        self.h_begin, self.h_end = self.bounds[self.rank]
+        self.group = group
+        self.ring = ring
+        self.timeout_s = float(timeout_s)
+        self.prev = (self.rank - 1) % self.world
+        self.next = (self.rank + 1) % self.world
+        self._gids: dict = {}
+        self._bufs: dict = {}
+
+    # ------------------------------------------------------------------ geometry
+    @property
+    def res(self) -> tuple[int, int, int]:
+        """The band's own resolution ``(C, H_band, W)``."""
+        C, _, W = self.field_res
+        return (C, self.h_end - self.h_begin, W)
+
+    def window_rows(self, window_size) -> tuple[int, int]:
+        ws, _ = maybe_adjust_windows(tuple(window_size), (0, 0, 0), self.field_res)
+        return self.h_begin // ws[1], self.h_end // ws[1]
+
+    def group_ids(self, window_size, shift_size, warped: bool, device) -> Optional[torch.Tensor]:
+        """The band's ``(nW_band, N)`` region ids, or ``None`` for an unshifted block."""
+        from .window_attn import shifted_window_group_ids
+
+        ws, ss = maybe_adjust_windows(tuple(window_size), tuple(shift_size), self.field_res)
+        if not any(ss):
+            return None
+        key = (ws, ss, bool(warped), str(device))
+        hit = self._gids.get(key)
+        if hit is None:
+            full = shifted_window_group_ids(self.field_res, tuple(window_size), tuple(shift_size), warped, device)
+            C, H, W = self.field_res
+            g1 = [-(-d // w) for d, w in zip((C, H, W), ws)]
+            a, b = self.h_begin // ws[1], self.h_end // ws[1]
+            hit = full.view(g1[0], g1[1], g1[2], -1)[:, a:b].reshape(-1, full.shape[-1]).contiguous()
+            self._gids[key] = hit
+        return hit
+
+    # ------------------------------------------------------------------ exchanges
+    def buffer(self, name: str, shape, dtype, device) -> torch.Tensor:
+        """Persistent receive/send buffer, reused across calls of the same shape."""
+        key = (name, tuple(shape), dtype, str(device))
+        buf = self._bufs.get(key)
+        if buf is None:
+            buf = torch.empty(shape, dtype=dtype, device=device)
+            self._bufs[key] = buf
+        return buf
+
+    def exchange(self, send: torch.Tensor, recv: torch.Tensor, dst: int, src: int) -> None:
+        """Send ``send`` to rank ``dst`` and receive ``recv`` from rank ``src``.
+
+        NCCL: both transfers are queued on NCCL's stream ordered after the current stream's work,
+        and the current stream waits for them; the host does not block. gloo: the host waits at
+        most ``timeout_s``. Failures raise :class:`HaloExchangeError`.
+        """
+        if self.world == 1:
+            recv.copy_(send)
+            return
+        if self.ring is not None:
+            self.ring.exchange(self.rank, send, recv, dst, src)
+            return
+        import torch.distributed as dist
+
+        try:
+            g = self.group
+            gdst = dst if g is None else dist.get_global_rank(g, dst)
+            gsrc = src if g is None else dist.get_global_rank(g, src)
+            works = dist.batch_isend_irecv([
+                dist.P2POp(dist.isend, send.contiguous(), gdst, g),
+                dist.P2POp(dist.irecv, recv, gsrc, g),
+            ])
+            cuda = recv.is_cuda
+            for w in works:
+                if cuda:
+                    w.wait()
+                else:
+                    w.wait(timedelta(seconds=self.timeout_s))
+        except HaloExchangeError:
+            raise
+        except RuntimeError as e:
+            raise HaloExchangeError(
+                f"rank {self.rank}: halo exchange (send to {dst}, receive from {src}) failed: {e}") from e
+
+    def halo_forward(self, x_band: torch.Tensor, s: int, dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        """Receive the next band's first ``s`` rows: ``x_band (B, C, Hb, W, D)`` -> ``(B, C, s, W, D)``.
+
+        This rank sends its own first ``s`` rows to the previous band at the same time.
+        """
+        B, C, _, W, D = x_band.shape
+        dtype = x_band.dtype if dtype is None else dtype
+        send = self.buffer("fwd_send", (B, C, s, W, D), dtype, x_band.device)
+        send.copy_(x_band[:, :, :s])
+        recv = self.buffer("fwd_recv", (B, C, s, W, D), dtype, x_band.device)
+        self.exchange(send, recv, dst=self.prev, src=self.next)
+        return recv
+
+    def halo_back(self, rows: torch.Tensor) -> torch.Tensor:
+        """Send the halo-back rows ``(B, C, s, W, D)`` to the next band; receive this band's own
+        first ``s`` rows, computed by the previous band."""
+        recv = self.buffer("back_recv", tuple(rows.shape), rows.dtype, rows.device)
+        self.exchange(rows, recv, dst=self.next, src=self.prev)
+        return recv
+
+
+def run_ranks(world: int, fn: Callable[[int, LocalRing], object], timeout_s: float = 120.0) -> list:
+    """Run ``fn(rank, ring)`` for ``world`` emulated ranks on threads of this process and return
+    their results in rank order; the first exception of any rank is re-raised."""
+    import threading
+
+    ring = LocalRing(world, timeout_s=timeout_s)
+    out: list = [None] * world
+    err: list = [None] * world
+
+    def body(r: int) -> None:
+        try:
+            out[r] = fn(r, ring)
+        except BaseException as e:  # noqa: BLE001 - re-raised in the caller
+            err[r] = e
+            ring._barrier.abort()
+
+    ts = [threading.Thread(target=body, args=(r,), daemon=True) for r in range(world)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(timeout_s)
+    for e in err:
+        if e is not None:
+            raise e
+    if any(t.is_alive() for t in ts):
+        raise HaloExchangeError(f"emulated ranks did not finish within {timeout_s} s")
+    return out

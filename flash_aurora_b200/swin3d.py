@@ -36,8 +36,13 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .adaln import adaptive_layernorm_film_add_residual_forward, unmerge_adaptive_layernorm_film_add_residual
-from .swin3d_layout import roll_pad_partition_windows
+from .adaln import (
+    adaptive_layernorm_film_add_residual_forward,
+    unmerge_adaptive_layernorm_film_add_residual,
+    unmerge_adaptive_layernorm_film_add_residual_band,
+)
+from .sharding import BandContext
+from .swin3d_layout import band_halo_extract, roll_pad_partition_windows, roll_pad_partition_windows_band
 from .util import maybe_adjust_windows
 from .window_attn import shifted_window_group_ids, window_attn_fwd_cute_qkvpacked
 from .workspace_pool import InferenceWorkspacePool
@@ -171,8 +176,14 @@ class Swin3DTransformerBlock(nn.Module):
         return self._bf16.get(lin.weight), (self._bf16.get(lin.bias) if lin.bias is not None else None)
 
     def forward(self, x: torch.Tensor, c: torch.Tensor, res, rollout_step: int = 0,
-                warped: bool = True) -> torch.Tensor:
-        """``x (B, C*H*W, D)`` fp32, ``c (B, ctx)`` -> ``(B, C*H*W, D)`` fp32."""
+                warped: bool = True, band: Optional[BandContext] = None) -> torch.Tensor:
+        """``x (B, C*H*W, D)`` fp32, ``c (B, ctx)`` -> ``(B, C*H*W, D)`` fp32.
+
+        With ``band`` (a :class:`~flash_aurora_b200.sharding.BandContext`), ``x`` and ``res`` are
+        this rank's latitude band of the field ``band.field_res``: the window geometry and mask are
+        the field's, a shifted block exchanges its half-window halo rows with the neighbouring
+        bands, and the result equals the band's rows of the unsharded block.
+        """
         if not x.is_cuda:
             raise RuntimeError("Swin3DTransformerBlock.forward requires CUDA tensors (no CPU path).")
         C, H, W = res
@@ -181,10 +192,16 @@ class Swin3DTransformerBlock(nn.Module):
         if x.dtype != torch.float32:
             x = x.float()
         x = x.contiguous()
-        ws, ss = maybe_adjust_windows(self.window_size, self.shift_size, res)
-        gids = None
-        if any(s != 0 for s in ss):
+        if band is not None and tuple(res) != band.res:
+            raise ValueError(f"res {tuple(res)} is not the band's resolution {band.res}")
+        field_res = band.field_res if band is not None else tuple(res)
+        ws, ss = maybe_adjust_windows(self.window_size, self.shift_size, field_res)
+        if band is not None:
+            gids = band.group_ids(self.window_size, self.shift_size, warped, x.device)
+        elif any(s != 0 for s in ss):
             gids = shifted_window_group_ids(tuple(res), self.window_size, self.shift_size, warped, x.device)
+        else:
+            gids = None
         bf16 = self.precision == "bf16_mixed"
         act = torch.bfloat16 if bf16 else torch.float32
         heads = self.num_heads
@@ -192,17 +209,32 @@ class Swin3DTransformerBlock(nn.Module):
         sh2, sc2 = self.norm2.modulation(c)
         eps = float(self.norm1.ln.eps)
         with _matmul_tf32(self.precision == "tf32"):
-            xw = roll_pad_partition_windows(x.view(B, C, H, W, D), res, self.window_size, self.shift_size,
-                                            out_dtype=act)
+            x5 = x.view(B, C, H, W, D)
+            if band is None:
+                xw = roll_pad_partition_windows(x5, res, self.window_size, self.shift_size, out_dtype=act)
+            else:
+                halo = band.halo_forward(x5, ss[1]) if ss[1] else None
+                xw = roll_pad_partition_windows_band(x5, halo, field_res, self.window_size, self.shift_size,
+                                                     out_dtype=act)
             wq, bq = self._w(self.attn.qkv, bf16)
             qkv = F.linear(xw, wq, bq)
             a = window_attn_fwd_cute_qkvpacked(qkv, heads, group_ids=gids, output_layout="bnc")
             wp, bp = self._w(self.attn.proj, bf16)
             a = F.linear(a, wp, bp)
             x1_bf16 = torch.empty(B, L, D, device=x.device, dtype=torch.bfloat16) if bf16 else None
-            x1 = unmerge_adaptive_layernorm_film_add_residual(
-                a, x, sc1, sh1, res, self.window_size, self.shift_size, float(self.norm1.scale_bias), eps,
-                out_bf16=x1_bf16)
+            if band is None:
+                x1 = unmerge_adaptive_layernorm_film_add_residual(
+                    a, x, sc1, sh1, res, self.window_size, self.shift_size, float(self.norm1.scale_bias), eps,
+                    out_bf16=x1_bf16)
+            else:
+                halo_in = None
+                if ss[1]:
+                    rows = band_halo_extract(a, res, field_res, self.window_size, self.shift_size,
+                                             out=band.buffer("back_send", (B, C, ss[1], W, D), a.dtype, a.device))
+                    halo_in = band.halo_back(rows)
+                x1 = unmerge_adaptive_layernorm_film_add_residual_band(
+                    a, halo_in, x, sc1, sh1, res, field_res, self.window_size, self.shift_size,
+                    float(self.norm1.scale_bias), eps, out_bf16=x1_bf16)
             w1, b1 = self._w(self.mlp.fc1, bf16)
             h = F.linear(x1_bf16 if bf16 else x1, w1, b1)
             h = F.gelu(h)
@@ -279,9 +311,14 @@ class BasicLayer3D(nn.Module):
         self.downsample = downsample(dim=dim) if downsample is not None else None
         self.upsample = upsample(dim=dim) if upsample is not None else None
 
-    def forward(self, x, c, res, crop=(0, 0, 0), rollout_step: int = 0):
+    def forward(self, x, c, res, crop=(0, 0, 0), rollout_step: int = 0,
+                band: Optional[BandContext] = None):
+        """``band``: run the blocks on this rank's latitude band of the stage's field (a stage
+        with a patch merge or split is not sharded: those change the band geometry)."""
+        if band is not None and (self.downsample is not None or self.upsample is not None):
+            raise ValueError("latitude-band sharding covers block stacks without patch merge/split")
         for blk in self.blocks:
-            x = blk(x, c, res, rollout_step)
+            x = blk(x, c, res, rollout_step, band=band)
         if self.downsample is not None:
             return self.downsample(x, res), x
         if self.upsample is not None:

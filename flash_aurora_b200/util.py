@@ -7,7 +7,7 @@ from functools import lru_cache
 
 from . import _lib
 
-__all__ = ["maybe_adjust_windows", "window_geometry"]
+__all__ = ["maybe_adjust_windows", "window_geometry", "band_geometry"]
 
 
 def maybe_adjust_windows(window_size, shift_size, res):
@@ -39,3 +39,22 @@ def window_geometry(res, window_size, shift_size):
                                 ctypes.byref(n))
     _lib.check(rc, "window_geometry")
     return tuple(ws), tuple(ss), tuple(pf), tuple(padded), int(nw.value), int(n.value)
+
+
+def band_geometry(band_res, field_res, window_size, shift_size):
+    """``(ws, ss, num_windows, window_tokens)`` of a latitude band ``(C, H_band, W)`` of the field
+    ``(C, H, W)``. Window clamping and shifts are decided on the field (as the unsharded block
+    does); the band must hold whole window rows and the field must need no H padding."""
+    band_res, field_res = tuple(int(v) for v in band_res), tuple(int(v) for v in field_res)
+    ws, ss, pf, padded, nW, N = window_geometry(field_res, tuple(window_size), tuple(shift_size))
+    C, Hb, W = band_res
+    if (C, W) != (field_res[0], field_res[2]):
+        raise ValueError(f"band {band_res} must share C and W with the field {field_res}")
+    H = field_res[1]
+    if padded[1] != H:
+        raise ValueError(f"band sharding needs H ({H}) to be a multiple of the window height ({ws[1]})")
+    if Hb <= 0 or Hb > H or Hb % ws[1]:
+        raise ValueError(f"band height {Hb} must be a positive multiple of {ws[1]}, at most {H}")
+    if ss[1] > Hb:
+        raise ValueError(f"halo of {ss[1]} rows is deeper than the band ({Hb} rows)")
+    return ws, ss, nW // (H // ws[1]) * (Hb // ws[1]), N

@@ -103,6 +103,46 @@ int fa_unmerge_adaln_film(const void* windows, int windows_dtype, const void* re
                           const int32_t window_size[3], const int32_t shift_size[3], void* stream);
 
 /*
+ * Latitude-band sharding of a field (C, H_field, W) across ranks: each rank holds a band of
+ * H_band whole window rows, x (B, C, H_band, W, D). No reference counterpart: the upstream
+ * backbone runs one field per device (its only multi-device path is a pipeline placement,
+ * engine/distributed/rollout_pipeline.py:137-169). window_size / shift_size are the field's;
+ * clamping is decided on the field, which must need no H padding. With an H shift s = ss[1],
+ * the band's shifted windows start s rows into the band:
+ *
+ *  - fa_roll_pad_partition_band: windows of the band; rows past the band are read from `halo`
+ *    (B, C, s, W, D), the next band's first s rows (cyclically: the last band takes band 0's).
+ *  - fa_band_halo_extract: halo_out (B, C, s, W, D) = the band's last s shifted rows, unrolled
+ *    in C and W; they are the next band's first s original rows (its halo-back buffer).
+ *  - fa_crop_roll_unmerge_band / fa_unmerge_adaln_film_band: inverse (plain, or fused with
+ *    AdaLN + residual as fa_unmerge_adaln_film); rows 0..s-1 of the band are read from `halo_in`
+ *    (B, C, s, W, D, windows dtype), the previous band's halo extract.
+ *
+ * Window order inside the band is (c1, h1, w1) over the band's own grid, so the band's windows
+ * are the rows [h1_begin, h1_end) of the field's window grid; region ids for a mask are sliced
+ * from the field's (nW, N) ids in the same way. With s = 0 the halo pointers may be NULL.
+ */
+int fa_roll_pad_partition_band(const void* x, const void* halo, int x_dtype, void* windows,
+                               int windows_dtype, int64_t B, int64_t C, int64_t H_band,
+                               int64_t H_field, int64_t W, int64_t D, const int32_t window_size[3],
+                               const int32_t shift_size[3], void* stream);
+int fa_band_halo_extract(const void* windows, int windows_dtype, void* halo_out, int halo_dtype,
+                         int64_t B, int64_t C, int64_t H_band, int64_t H_field, int64_t W,
+                         int64_t D, const int32_t window_size[3], const int32_t shift_size[3],
+                         void* stream);
+int fa_crop_roll_unmerge_band(const void* windows, const void* halo_in, int windows_dtype,
+                              void* out, int out_dtype, int64_t B, int64_t C, int64_t H_band,
+                              int64_t H_field, int64_t W, int64_t D, const int32_t window_size[3],
+                              const int32_t shift_size[3], void* stream);
+int fa_unmerge_adaln_film_band(const void* windows, const void* halo_in, int windows_dtype,
+                               const void* residual, int residual_dtype, const void* scale,
+                               const void* shift, int mod_dtype, float scale_bias, float eps,
+                               void* out, int out_dtype, void* out_bf16, int64_t B, int64_t C,
+                               int64_t H_band, int64_t H_field, int64_t W, int64_t D,
+                               const int32_t window_size[3], const int32_t shift_size[3],
+                               void* stream);
+
+/*
  * Shifted-window region ids of every window token, (nW, N) uint8 written to HOST memory.
  * Tokens i, j of a window attend to each other unmasked iff their ids are equal; otherwise the
  * logit gets the upstream -100 (compute_3d_shifted_window_mask, swin3d.py:526-599, with the

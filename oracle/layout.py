@@ -12,6 +12,10 @@ Upstream semantics restated (paths relative to the Flash-Aurora project):
 * window merge -> crop -> roll(+ss)   flash_aurora/aurora/model/swin3d.py:775-789, 454-485;
                                       kernel ops/triton_swin3d_layout.py:253-307
 * shifted-window mask groups          flash_aurora/aurora/model/swin3d.py:526-599
+
+Latitude bands (a field split along H across ranks) have no upstream counterpart; the band
+functions below restate them from the field definitions above by explicit concatenation, an
+independent formulation of the index encoding used by the CUDA band kernels.
 """
 
 from __future__ import annotations
@@ -193,3 +197,61 @@ def shifted_window_mask(res, window_size, shift_size, warped: bool = True) -> np
     gid = window_group_ids(res, window_size, shift_size, warped).astype(np.int64)
     diff = gid[:, None, :] - gid[:, :, None]
     return np.where(diff != 0, MASKED_BIAS, 0.0).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------------------------
+# Latitude bands
+# ---------------------------------------------------------------------------------------------
+
+
+def band_split(field_res, window_size, world: int):
+    """Token-row ranges of ``world`` bands of whole window rows (first bands get the smaller share)."""
+    C, H, W = field_res
+    ws, _ = maybe_adjust_windows(tuple(window_size), (0, 0, 0), tuple(field_res))
+    rows = H // ws[1]
+    assert H % ws[1] == 0 and 1 <= world <= rows
+    cuts = [(r * rows) // world for r in range(world + 1)]
+    return [(cuts[r] * ws[1], cuts[r + 1] * ws[1]) for r in range(world)]
+
+
+def _band_shifts(field_res, window_size, shift_size):
+    ws, ss = maybe_adjust_windows(tuple(window_size), tuple(shift_size), tuple(field_res))
+    return ws, ss
+
+
+def band_windows_of_field(windows_field: np.ndarray, field_res, window_size, shift_size, h_begin, h_end):
+    """Rows ``[h_begin, h_end)`` (token rows) of the field's window grid: ``(B*nW_band, N, D)``."""
+    g = geometry(field_res, window_size, shift_size)
+    C1, H1, W1 = g.grid
+    BnW, N, D = windows_field.shape
+    B = BnW // g.num_windows
+    v = windows_field.reshape(B, C1, H1, W1, N, D)[:, :, h_begin // g.ws[1]:h_end // g.ws[1]]
+    return np.ascontiguousarray(v).reshape(-1, N, D)
+
+
+def band_partition(x_band: np.ndarray, halo, field_res, window_size, shift_size) -> np.ndarray:
+    """Windows of one band: rows ``s..`` of the band followed by the ``s`` halo rows (the next
+    band's first rows) form the band's shifted rows; C and W are shifted as in the field."""
+    ws, ss = _band_shifts(field_res, window_size, shift_size)
+    B, C, Hb, W, D = x_band.shape
+    s = ss[1]
+    ext = np.concatenate([x_band[:, :, s:], halo], axis=2) if s else x_band
+    return roll_pad_partition(ext, (C, Hb, W), ws, (ss[0], 0, ss[2]))
+
+
+def band_halo_extract(windows_band: np.ndarray, band_res, field_res, window_size, shift_size) -> np.ndarray:
+    """The band's last ``s`` shifted rows, un-rolled in C and W: ``(B, C, s, W, D)``."""
+    ws, ss = _band_shifts(field_res, window_size, shift_size)
+    ext = crop_roll_unmerge(windows_band, tuple(band_res), ws, (ss[0], 0, ss[2]))
+    return ext[:, :, band_res[1] - ss[1]:]
+
+
+def band_unmerge(windows_band: np.ndarray, halo_in, band_res, field_res, window_size, shift_size) -> np.ndarray:
+    """Inverse of :func:`band_partition`: ``(B, C, H_band, W, D)``; rows ``0..s-1`` come from
+    ``halo_in`` (the previous band's :func:`band_halo_extract`)."""
+    ws, ss = _band_shifts(field_res, window_size, shift_size)
+    s = ss[1]
+    ext = crop_roll_unmerge(windows_band, tuple(band_res), ws, (ss[0], 0, ss[2]))
+    if not s:
+        return ext
+    return np.concatenate([halo_in, ext[:, :, :band_res[1] - s]], axis=2)

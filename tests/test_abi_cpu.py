@@ -88,3 +88,29 @@ def test_invalid_arguments_return_status_without_a_gpu(lib):
     assert rc == _lib.FA_ERR_UNSUPPORTED and b"2048" in lib.fa_last_error()
     rc = lib.fa_adaln_film(p, 0, p, 1, p, p, 0, 0.0, 1e-5, p, 0, None, 1, 4, 256, None)
     assert rc == _lib.FA_ERR_INVALID and b"residual" in lib.fa_last_error()
+
+
+def test_band_arguments_return_status_without_a_gpu(lib):
+    from flash_aurora_b200 import _lib
+    ws, ss = _lib.i32x3((2, 6, 12)), _lib.i32x3((1, 3, 6))
+    p = ctypes.c_void_p(1 << 20)
+    # band height not a whole number of window rows
+    rc = lib.fa_roll_pad_partition_band(p, p, 0, p, 0, 1, 4, 9, 36, 72, 64, ws, ss, None)
+    assert rc == _lib.FA_ERR_INVALID and b"band height" in lib.fa_last_error()
+    # field height needing padding along H
+    rc = lib.fa_roll_pad_partition_band(p, p, 0, p, 0, 1, 4, 6, 45, 90, 64, ws, ss, None)
+    assert rc == _lib.FA_ERR_UNSUPPORTED and b"multiple of the window height" in lib.fa_last_error()
+    # shifted band without its halo
+    rc = lib.fa_roll_pad_partition_band(p, None, 0, p, 0, 1, 4, 12, 36, 72, 64, ws, ss, None)
+    assert rc == _lib.FA_ERR_INVALID and b"halo" in lib.fa_last_error()
+    rc = lib.fa_crop_roll_unmerge_band(p, None, 0, p, 0, 1, 4, 12, 36, 72, 64, ws, ss, None)
+    assert rc == _lib.FA_ERR_INVALID and b"halo" in lib.fa_last_error()
+    rc = lib.fa_unmerge_adaln_film_band(p, None, 0, p, 0, p, p, 0, 0.0, 1e-5, p, 0, None,
+                                        1, 4, 12, 36, 72, 64, ws, ss, None)
+    assert rc == _lib.FA_ERR_INVALID and b"halo" in lib.fa_last_error()
+    # band taller than the field
+    rc = lib.fa_band_halo_extract(p, 0, p, 0, 1, 4, 42, 36, 72, 64, ws, ss, None)
+    assert rc == _lib.FA_ERR_INVALID
+    # an unshifted band needs no halo and nothing is extracted (no launch, so no GPU needed)
+    z = _lib.i32x3((0, 0, 0))
+    assert lib.fa_band_halo_extract(p, 0, p, 0, 1, 4, 12, 36, 72, 64, ws, z, None) == _lib.FA_OK
