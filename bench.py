@@ -15,7 +15,10 @@ latent grid (4,180,360), batch 1) in the ``bf16_mixed`` tier, random init ~N(0, 
                  block per stage, extrapolated to the 48-block step (rank 0, N = 1 only).
 
 Multi-GPU (``torchrun --nproc-per-node N``): every rank runs its own backbone step on its own
-input (independent ensemble members, no data-path collective): weak scaling, replicas.
+input (independent ensemble members, no data-path collective): weak scaling, replicas. The
+line also carries ``sharded_config5``: BASELINE config 5 (a (4,360,720) x 512 Swin3D stage of
+10 blocks) split into latitude bands across the N ranks with the NCCL point-to-point halo
+exchange, strong scaling (``--no-sharded`` skips it; ``--workload sharded`` runs it alone).
 
 ``--impl reference`` times the reference algorithm on the host CPU instead (the CPU oracle, see
 above; rank 0 only) and prints the same metric.
@@ -269,10 +272,81 @@ def run_b200(args) -> None:
                      "launches": attn_launches, "kernel_ms_per_step": round(attn_ms / args.steps, 3)},
         "clocks": clocks,
     }
+    del model, x, y, yy
+    torch.cuda.empty_cache()
+    if not args.no_sharded:
+        line["sharded_config5"] = measure_sharded(dist, rank, world, local, min(args.steps, 5), 3)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample()
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------------------------
+# Config 5: a high-resolution Swin3D stage sharded by latitude bands across the ranks.
+# ----------------------------------------------------------------------------------------------
+CONFIG5 = dict(field=(4, 360, 720), dim=512, heads=8, depth=10, window=(2, 6, 12))
+
+
+def measure_sharded(dist, rank, world, local, steps, warmup) -> dict:
+    """Config 5 on ``world`` ranks: field (4,360,720) x 512, 8 heads, 10 blocks alternating
+    unshifted/shifted, bf16_mixed; rank r holds latitude band r and exchanges its 3-row halo with
+    its neighbours over NCCL for every shifted block. Strong scaling: the field is fixed."""
+    from flash_aurora_b200.sharding import BandContext
+    from flash_aurora_b200.swin3d import BasicLayer3D
+
+    dev = torch.device("cuda", local)
+    cfg = CONFIG5
+    C, H, W = cfg["field"]
+    D = cfg["dim"]
+    torch.manual_seed(4321)  # identical weights on every rank
+    layer = BasicLayer3D(dim=D, depth=cfg["depth"], num_heads=cfg["heads"], ws=cfg["window"], time_dim=D,
+                         precision="bf16_mixed")
+    with torch.no_grad():
+        for p in layer.parameters():
+            p.normal_(0.0, 0.02)
+    layer = layer.to(dev).eval()
+    group = dist.group.WORLD if dist is not None else None
+    ctx = BandContext(cfg["field"], cfg["window"], rank, world, group=group, timeout_s=120)
+    gen = torch.Generator(device=dev).manual_seed(99 + rank)
+    Cb, Hb, Wb = ctx.res
+    xb = torch.randn(1, Cb * Hb * Wb, D, device=dev, generator=gen)
+    c = torch.randn(1, D, device=dev, generator=torch.Generator(device=dev).manual_seed(98))
+    with torch.no_grad():
+        for _ in range(warmup):
+            y, _ = layer(xb, c, ctx.res, band=ctx)
+        _barrier(dist)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            y, _ = layer(xb, c, ctx.res, band=ctx)
+        e1.record()
+        _barrier(dist)
+    ms = _max_over_ranks(dist, e0.elapsed_time(e1) / steps)
+    shifted = cfg["depth"] // 2
+    halo_fwd = C * 3 * W * D * 4 if world > 1 else 0  # fp32 rows to the previous band
+    halo_back = C * 3 * W * D * 2 if world > 1 else 0  # bf16 rows to the next band
+    nw = C // 2 * (H // 6) * (W // 12)
+    flops_block = 2 * C * H * W * D * (3 * D + D + 8 * D) + 4 * nw * cfg["heads"] * 144 * 144 * (D // cfg["heads"])
+    del layer, xb, y
+    torch.cuda.empty_cache()
+    return {"workload": "config5: Swin3D stage, field (4,360,720) x 512, 8 heads, 10 blocks (5 shifted), "
+                        "bf16_mixed, latitude bands of window rows, NCCL P2P 3-row halo per shifted block",
+            "ms_per_step": round(ms, 3), "windows_per_s": round(nw * cfg["depth"] / (ms * 1e-3), 1),
+            "tflops": round(flops_block * cfg["depth"] / (ms * 1e-3) / 1e12, 1),
+            "bands": [list(b) for b in ctx.bounds], "scaling": "strong",
+            "halo_bytes_per_rank_per_step": shifted * (halo_fwd + halo_back), "steps": steps, "warmup": warmup}
+
+
+def run_sharded(args) -> None:
+    dist, rank, world, local = _dist()
+    torch.cuda.set_device(local)
+    out = measure_sharded(dist, rank, world, local, args.steps, args.warmup)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -375,7 +449,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["backbone", "attention", "layout_adaln"], default="backbone")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the config-5 sharded-stage object")
+    ap.add_argument("--workload", choices=["backbone", "attention", "layout_adaln", "sharded"], default="backbone")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -383,6 +458,8 @@ def main() -> None:
         return run_attention(args)
     if args.workload == "layout_adaln":
         return run_layout_adaln(args)
+    if args.workload == "sharded" and args.impl != "reference":
+        return run_sharded(args)
     if args.impl == "reference":
         run_reference(args)
     else:
