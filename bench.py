@@ -355,6 +355,22 @@ def run_sharded(args) -> None:
 # ----------------------------------------------------------------------------------------------
 # Kernel-level workloads (BASELINE configs 2 and 3); not the driver's default line.
 # ----------------------------------------------------------------------------------------------
+class L2Flush:
+    """Empties L2 between timed launches: writes a 256 MB buffer (twice L2), then reads another
+    256 MB buffer so that the flush's dirty lines are written back before the timed launch
+    instead of during it."""
+
+    def __init__(self, device) -> None:
+        n = 256 * 1024 * 1024 // 4
+        self.w = torch.empty(n, device=device)
+        self.r = torch.zeros(n, device=device)
+        self.sink = torch.empty((), device=device)
+
+    def __call__(self) -> None:
+        self.w.zero_()
+        torch.sum(self.r, dim=0, out=self.sink)
+
+
 def _time_launches(fn, iters, warmup=3, flush=None):
     """Average device ms per call, CUDA events on the current stream, L2 flushed between calls."""
     for _ in range(warmup):
@@ -363,7 +379,7 @@ def _time_launches(fn, iters, warmup=3, flush=None):
     total = 0.0
     for _ in range(iters):
         if flush is not None:
-            flush.zero_()
+            flush()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         fn()
@@ -379,7 +395,7 @@ def run_attention(args) -> None:
     import flash_aurora_b200 as fa
     dev = torch.device("cuda", 0)
     hbm, tflops_peak, kind = _peaks()
-    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    flush = L2Flush(dev)
     g = torch.Generator(device=dev).manual_seed(0)
     res, ws, ss = (4, 180, 360), (2, 6, 12), (1, 3, 6)
     Bwin, H, N, Dh = 1800, 8, 144, 64
@@ -408,7 +424,7 @@ def run_layout_adaln(args) -> None:
     import flash_aurora_b200 as fa
     dev = torch.device("cuda", 0)
     hbm, _, kind = _peaks()
-    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    flush = L2Flush(dev)
     g = torch.Generator(device=dev).manual_seed(0)
     res, ws, ss = (4, 45, 90), (2, 6, 12), (1, 3, 6)
     C, H, W = res
@@ -433,6 +449,12 @@ def run_layout_adaln(args) -> None:
          lambda: fa.unmerge_adaptive_layernorm_film_add_residual(win, resid, scale, shift, res, ws, ss),
          L * D * (4 + 4 + 4)),
     ]
+    # The MLP activation at stage 1 of config 4: fc1 output (259200, 2048) bf16, in place.
+    h = torch.randn(259200, 2048, device=dev, generator=g).bfloat16()
+    cases.append(("mlp exact GELU, S1 fc1 output (259200, 2048) bf16, in place",
+                  lambda: fa.gelu_erf(h, inplace=True), h.numel() * 2 * 2))
+    cases.append(("[torch F.gelu on the same tensor, for comparison]",
+                  lambda: torch.nn.functional.gelu(h), h.numel() * 2 * 2))
     for name, fn, nbytes in cases:
         ms = _time_launches(fn, args.steps, flush=flush)
         gbs = nbytes / (ms * 1e-3) / 1e9

@@ -15,6 +15,7 @@ PyTorch host layer that mirrors the operator interface of upstream Flash-Aurora:
 * ``sharding``       latitude-band window sharding with a point-to-point halo exchange
 """
 
+from .activation import gelu_erf
 from .adaln import (
     adaptive_layernorm_film_add_residual_forward,
     adaptive_layernorm_film_forward,
@@ -42,6 +43,7 @@ from .window_attn import (
 from .workspace_pool import InferenceWorkspacePool
 
 __all__ = [
+    "gelu_erf",
     "adaptive_layernorm_film_add_residual_forward",
     "adaptive_layernorm_film_forward",
     "unmerge_adaptive_layernorm_film_add_residual",

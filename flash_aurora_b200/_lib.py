@@ -43,6 +43,7 @@ SIGNATURES = {
                                          _i32p, _i32p, _vp]),
     "fa_unmerge_adaln_film_band": (_i32, [_vp, _vp, _i32, _vp, _i32, _vp, _vp, _i32, _f32, _f32, _vp, _i32, _vp,
                                           _i64, _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
+    "fa_gelu_erf": (_i32, [_vp, _vp, _i32, _i64, _vp]),
     "fa_shifted_window_groups": (_i32, [_i64, _i64, _i64, _i32p, _i32p, _i32, _u8p]),
     "fa_window_attention": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64p, _u8p, _u8p, _i64, _f32, _vp]),
     "fa_window_attention_qkvpacked": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _u8p, _u8p, _i64, _f32, _vp]),

@@ -15,7 +15,7 @@ Per block (upstream swin3d.py:706-815, post-norm), precision ``"bf16_mixed"``:
 4. proj linear, bf16 (cuBLAS).
 5. ``fa_unmerge_adaln_film``: crop/un-roll/merge of the proj output fused into
    ``x1 = x + AdaLN1(.)`` (fp32), plus a bf16 copy of ``x1`` for fc1.
-6. fc1 (bf16) -> exact GELU -> fc2 (bf16).
+6. fc1 (bf16) -> exact GELU (``fa_gelu_erf``, in place) -> fc2 (bf16).
 7. ``fa_adaln_film``: ``x2 = x1 + AdaLN2(h)`` (bf16 input, fp32 residual and output).
 
 Every rounding point equals the upstream ``bf16_mixed`` tier (custom_op_paths.py:188-263): the
@@ -41,6 +41,7 @@ from .adaln import (
     unmerge_adaptive_layernorm_film_add_residual,
     unmerge_adaptive_layernorm_film_add_residual_band,
 )
+from .activation import gelu_erf
 from .sharding import BandContext
 from .swin3d_layout import band_halo_extract, roll_pad_partition_windows, roll_pad_partition_windows_band
 from .util import maybe_adjust_windows
@@ -237,7 +238,7 @@ class Swin3DTransformerBlock(nn.Module):
                     float(self.norm1.scale_bias), eps, out_bf16=x1_bf16)
             w1, b1 = self._w(self.mlp.fc1, bf16)
             h = F.linear(x1_bf16 if bf16 else x1, w1, b1)
-            h = F.gelu(h)
+            h = gelu_erf(h, inplace=True)
             w2, b2 = self._w(self.mlp.fc2, bf16)
             h = F.linear(h, w2, b2)
             return adaptive_layernorm_film_add_residual_forward(

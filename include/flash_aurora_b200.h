@@ -143,6 +143,14 @@ int fa_unmerge_adaln_film_band(const void* windows, const void* halo_in, int win
                                void* stream);
 
 /*
+ * Exact GELU, out[i] = x[i] * 0.5 * (1 + erf(x[i] / sqrt(2))) in fp32, rounded to dtype
+ * (FA_F32 | FA_BF16); n elements, contiguous; out == x (in place) is allowed, any other overlap is
+ * rejected. Replaces the nn.GELU() between fc1 and fc2 of the block MLP (swin3d.py:73-109), which
+ * upstream runs as a PyTorch elementwise kernel.
+ */
+int fa_gelu_erf(const void* x, void* out, int dtype, int64_t n, void* stream);
+
+/*
  * Shifted-window region ids of every window token, (nW, N) uint8 written to HOST memory.
  * Tokens i, j of a window attend to each other unmasked iff their ids are equal; otherwise the
  * logit gets the upstream -100 (compute_3d_shifted_window_mask, swin3d.py:526-599, with the
