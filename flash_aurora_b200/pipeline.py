@@ -1,0 +1,87 @@
+"""Host-resident inputs and outputs streamed through a device step with overlapped copies.
+
+A forecast service feeds the backbone one field after another (ensemble members, or successive
+rollout inputs) from pinned host memory and reads every result back. Run serially, each step
+pays its host-to-device copy, the step, and its device-to-host copy one after another; the
+copies use the copy engines, not the SMs, so they can run under the neighbouring steps.
+:class:`HostPipeline` double-buffers the device input: step ``i + 1``'s upload runs on one copy
+stream while step ``i`` computes, and step ``i``'s download runs on another copy stream while
+step ``i + 1`` computes. Every step still moves its own input and output across PCIe; only the
+waiting is removed. Ordering is by CUDA events only; the host never blocks inside ``run``.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Sequence
+
+import torch
+
+__all__ = ["HostPipeline"]
+
+
+class HostPipeline:
+    """``run(host_inputs, host_outputs)`` computes ``host_outputs[i] = step(host_inputs[i])``.
+
+    ``step`` takes a device tensor shaped like the inputs and returns a device tensor shaped like
+    the outputs; it runs on the caller's current stream. Inputs and outputs should be pinned
+    host tensors (pageable memory works but serialises the copies).
+    """
+
+    def __init__(self, step: Callable[[torch.Tensor], torch.Tensor], device, depth: int = 2) -> None:
+        if depth < 1:
+            raise ValueError("depth must be >= 1")
+        self.step = step
+        self.device = torch.device(device)
+        self.depth = depth
+        self.up = torch.cuda.Stream(self.device)
+        self.down = torch.cuda.Stream(self.device)
+        self._bufs: list[torch.Tensor] = []
+
+    def _buffers(self, like: torch.Tensor) -> list[torch.Tensor]:
+        if not self._bufs or self._bufs[0].shape != like.shape or self._bufs[0].dtype != like.dtype:
+            self._bufs = [torch.empty(like.shape, dtype=like.dtype, device=self.device) for _ in range(self.depth)]
+        return self._bufs
+
+    def run(self, host_inputs: Sequence[torch.Tensor], host_outputs: Sequence[torch.Tensor]) -> None:
+        if len(host_inputs) != len(host_outputs):
+            raise ValueError("need one output tensor per input tensor")
+        n = len(host_inputs)
+        if n == 0:
+            return
+        compute = torch.cuda.current_stream(self.device)
+        bufs = self._buffers(host_inputs[0])
+        uploaded = [torch.cuda.Event() for _ in range(n)]
+        consumed = [torch.cuda.Event() for _ in range(n)]  # step i no longer reads its input buffer
+        start = torch.cuda.Event()
+        start.record(compute)
+        self.up.wait_event(start)
+        self.down.wait_event(start)
+
+        def upload(i: int) -> None:
+            with torch.cuda.stream(self.up):
+                if i >= self.depth:
+                    self.up.wait_event(consumed[i - self.depth])
+                bufs[i % self.depth].copy_(host_inputs[i], non_blocking=True)
+                uploaded[i].record(self.up)
+
+        for i in range(min(self.depth - 1, n)):
+            upload(i)
+        last_down = None
+        for i in range(n):
+            if i + self.depth - 1 < n:
+                upload(i + self.depth - 1)
+            compute.wait_event(uploaded[i])
+            y = self.step(bufs[i % self.depth])
+            consumed[i].record(compute)
+            done = torch.cuda.Event()
+            done.record(compute)
+            with torch.cuda.stream(self.down):
+                self.down.wait_event(done)
+                y.record_stream(self.down)
+                host_outputs[i].copy_(y, non_blocking=True)
+                last_down = torch.cuda.Event()
+                last_down.record(self.down)
+            del y
+        # The caller's stream ends after the last download, so events recorded on it after
+        # run() returns bracket all the copies.
+        compute.wait_event(last_down)
