@@ -424,8 +424,12 @@ attn_sync_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
 //                written to global memory as bf16.
 //   warp 3       rows 128..143 from S2/O2 TMEM lanes 96..111 / 112..127 with 16x256b loads (16 rows spread
 //                over the 32 threads, two rows per thread, reductions over 4-thread quads).
-// The shifted-window mask is turned into a bit per key once per window and reused by its heads; a
-// window with a single region skips masking. Every wait is bounded (status word + abort flag).
+// The shifted-window mask (region ids) goes through the tensor cores: warp 0 writes, once per
+// window, one-hot region operands (32-byte swizzle) and the S UMMAs get one more K=16 step that
+// raises every same-region logit by 100/scale, which the softmax cannot tell from upstream's -100
+// on the other pairs. Windows with one region skip it; id sets it cannot express (more than 16
+// regions, ids >= 32) and byte masks fall back to a bit per key. P keys 128..143 live in a
+// 32-byte-swizzled chunk to make room. Every wait is bounded (status word + abort flag).
 // ------------------------------------------------------------------------------------------
 namespace tc {
 
@@ -433,14 +437,20 @@ constexpr int kStages = 3;
 constexpr int kQKBytes = 2 * kTileBytes;  // Q and K of a tile (bf16, 144 x 128 B each)
 constexpr int kVBytes = kTileBytes;       // V of a tile
 constexpr int kStageBytes = kQKBytes + kVBytes;
-constexpr int kPChunk = kTileBytes;          // 64 keys x 144 rows of bf16
-constexpr int kPBytes = 3 * kPChunk;         // keys 0-63, 64-127, 128-143 (+ unused tail)
+constexpr int kPChunk = kTileBytes;          // 64 keys x 144 rows of bf16 (128-byte swizzle)
+constexpr int kRow32 = kMaxN * 32;           // 144 rows x 32 bytes (16 bf16, 32-byte swizzle)
+// P: keys 0-63 and 64-127 in 128-byte-swizzled chunks, keys 128-143 in a 32-byte-swizzled chunk.
+constexpr int kPBytes = 2 * kPChunk + kRow32;
+// One-hot region operands of a window's mask UMMA (A: queries, B: keys), two windows in flight.
+constexpr int kMaskOpBytes = 2 * kRow32;
+constexpr int kMaskBytes = 2 * kMaskOpBytes;
 constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // {max, sum} x warpgroup x row
 constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColS2 = 160, kColO0 = 320, kColO1 = 384, kColO2 = 448;
-constexpr int kNumBars = 28;
-constexpr int kSmem = kStages * kStageBytes + kPBytes + kXchgBytes + kNumBars * 8 + 16 + 1024;
+constexpr int kNumBars = 32;
+constexpr int kSmem = kStages * kStageBytes + kPBytes + kMaskBytes + kXchgBytes + kNumBars * 8 + 16 + 16 + 1024;
+static_assert(kSmem <= 227 * 1024, "shared memory budget");
 constexpr uint32_t kIdescS = ptx::make_idesc(1, 128, kMaxN, false, false);
 constexpr uint32_t kIdescO = ptx::make_idesc(1, 128, 64, false, true);
 // Rows 128..143 go through M=64 UMMAs over rows 80..143: A rows 48..63 land in TMEM lanes 96..111
@@ -448,10 +458,46 @@ constexpr uint32_t kIdescO = ptx::make_idesc(1, 128, 64, false, true);
 constexpr uint32_t kIdescS2 = ptx::make_idesc(1, 64, kMaxN, false, false);
 constexpr uint32_t kIdescO2 = ptx::make_idesc(1, 64, 64, false, true);
 constexpr uint32_t kRowOff80 = 80 * 128;  // 80 rows of a 128-byte-row tile (swizzle-atom aligned)
+constexpr uint32_t kRowOff80_32 = 80 * 32;  // the same in a 32-byte-row tile (256-byte atoms)
 constexpr uint32_t kLaneHalf = 16u << 16;
 
 enum { kFullQK = 0, kEmptyQK = 3, kFullV = 6, kEmptyV = 9, kSFull = 12, kSFree = 13, kPFull = 14, kPEmpty = 15,
-       kOFull = 16, kOFree = 18, kO2Full = 20, kO2Free = 22, kDone = 24, kXMax = 25, kXSum = 26 };
+       kOFull = 16, kOFree = 18, kO2Full = 20, kO2Free = 22, kDone = 24, kXMax = 25, kXSum = 26,
+       kMaskFull = 27, kMaskEmpty = 29 };
+
+// Byte offset of bf16 element e (0..15) of row r in a 32-byte-swizzled K-major tile.
+__device__ __forceinline__ uint32_t sw32_offset(int r, int e) {
+  return (uint32_t)(r * 32 + ((((e >> 3) ^ (r >> 2)) & 1) << 4) + (e & 7) * 2);
+}
+
+// How a window's region mask is applied. The region ids of a window are ranked among the ids
+// present (a 32-bit presence set); with 2..16 distinct ids below 32 the mask is one extra UMMA
+// K-step: A[q] = bias * onehot(rank(q)), B[k] = onehot(rank(k)), which adds `bias` (= 100 / scale,
+// the upstream -100 after scaling, in the raw logit domain) to every same-region pair. Adding it
+// to the same-region pairs instead of subtracting it from the others shifts each row of logits by
+// a constant, which the softmax cancels. Other id sets fall back to a per-logit mask.
+enum { kModeNone = 0, kModeUmma = 1, kModeBits = 2 };
+
+struct WindowRegions {
+  uint32_t present;  // bit i: region id i occurs in the window (ids < 32)
+  int mode;
+};
+
+// Warp-cooperative: all 32 lanes must call it with the same window.
+__device__ __forceinline__ WindowRegions window_regions(const uint8_t* gi, int N, int lane) {
+  uint32_t pres = 0u, over = 0u;
+  for (int k = lane; k < N; k += 32) {
+    const uint32_t id = __ldg(gi + k);
+    if (id < 32u) pres |= 1u << id; else over = 1u;
+  }
+  pres = __reduce_or_sync(0xffffffffu, pres);
+  over = __reduce_or_sync(0xffffffffu, over);
+  const int distinct = __popc(pres);
+  WindowRegions r;
+  r.present = pres;
+  r.mode = over || distinct > 16 ? kModeBits : (distinct > 1 ? kModeUmma : kModeNone);
+  return r;
+}
 
 __device__ __forceinline__ uint32_t nibble_of_bytes(uint32_t ne) {
   return (ne & 1u) | ((ne >> 7) & 2u) | ((ne >> 14) & 4u) | ((ne >> 21) & 8u);
@@ -474,7 +520,9 @@ __device__ __forceinline__ void row_mask_bits(const Params& p, int mw, int row, 
       src = p.mask + ((int64_t)mw * p.N + row) * p.N;
     }
     if ((p.N & 15) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-      for (int v = 0; v < p.N / 16; ++v) {
+#pragma unroll
+      for (int v = 0; v < kMaxN / 16; ++v) {
+        if (v >= p.N / 16) break;
         const uint4 w = __ldg(reinterpret_cast<const uint4*>(src) + v);
         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -535,7 +583,7 @@ __device__ __forceinline__ float raw_logits72(uint32_t (&v)[72], const uint32_t 
   return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
 }
 
-template <int kMask>
+template <int kMask, bool kFullN>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                     const __grid_constant__ CUtensorMap tmv, const Params p) {
@@ -543,9 +591,11 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t sP = sbase + kStages * kStageBytes;
-  float* xchg = reinterpret_cast<float*>(smem + kStages * kStageBytes + kPBytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kPBytes + kXchgBytes);
+  const uint32_t sMask = sP + kPBytes;  // 256-byte aligned (32-byte-swizzle atoms)
+  float* xchg = reinterpret_cast<float*>(smem + kStages * kStageBytes + kPBytes + kMaskBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kPBytes + kMaskBytes + kXchgBytes);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* mask_mode = reinterpret_cast<volatile int*>(tmem_holder + 4);  // per mask buffer
   const uint32_t bar0 = smem_u32(bars);
   auto BAR = [&](int slot) -> uint32_t { return bar0 + 8u * (uint32_t)slot; };
   __shared__ int abort_flag;
@@ -579,6 +629,10 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
     mbar_init(BAR(kDone), 1);
     mbar_init(BAR(kXMax), 8);  // row-max exchange between the two softmax warpgroups
     mbar_init(BAR(kXSum), 8);  // row-sum exchange
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(BAR(kMaskFull + b), 1);
+      mbar_init(BAR(kMaskEmpty + b), 1);
+    }
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -590,40 +644,91 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   volatile int* abort = &abort_flag;
-  const bool full_n = p.N == kMaxN;
   const float braw = kMaskedLog2 / p.scale_log2;  // -100 / scale: the mask bias before scaling
 
   if (warp == 0 || warp == 2) {
     // ---------------- TMA producers: warp 0 loads Q and K, warp 2 loads V ----------------
     // Q/K slots are released as soon as the S UMMAs of their tile complete, V slots after PV, so
-    // the Q/K loads of later tiles do not wait for the PV of earlier ones.
+    // the Q/K loads of later tiles do not wait for the PV of earlier ones. Warp 0 also builds the
+    // one-hot region operands of each window's mask UMMA (all 32 lanes) before its first load.
+    const bool qk = warp == 0;
+    const int full0 = qk ? kFullQK : kFullV, empty0 = qk ? kEmptyQK : kEmptyV;
+    const uint32_t bytes = qk ? (uint32_t)kQKBytes : (uint32_t)kVBytes;
     if (lane == 0) {
-      const bool qk = warp == 0;
-      const int full0 = qk ? kFullQK : kFullV, empty0 = qk ? kEmptyQK : kEmptyV;
-      const uint32_t bytes = qk ? (uint32_t)kQKBytes : (uint32_t)kVBytes;
       if (qk) {
         tma_prefetch_desc(&tmq);
         tma_prefetch_desc(&tmk);
       } else {
         tma_prefetch_desc(&tmv);
       }
-      int last_par[kStages] = {-1, -1, -1};
-      for (int i = 0; i < n_local; ++i) {
-        const int t = t_begin + i;
+    }
+    int last_par[kStages] = {-1, -1, -1};
+    int cur_w = -1, wseq = -1;
+    // The mask bias of same-region pairs in the raw logit domain, as a bf16 operand value.
+    const uint32_t bias_bits = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(-braw));
+    for (int i = 0; i < n_local; ++i) {
+      const int t = t_begin + i;
+      const int w = t / p.H, h = t - w * p.H;
+      if constexpr (kMask == kGroups) {
+        if (qk && w != cur_w) {
+          cur_w = w;
+          ++wseq;
+          const int mb = wseq & 1;
+          const uint32_t u = (uint32_t)(wseq >> 1);
+          int okw = 1;
+          if (lane == 0) okw = mbar_wait(BAR(kMaskEmpty + mb), (u & 1u) ^ 1u, abort, p.status, 13, kTimeoutNs);
+          if (!__shfl_sync(0xffffffffu, okw, 0)) break;
+          const uint8_t* gi = p.mask + (int64_t)(w % p.nW) * p.N;
+          const WindowRegions wr = window_regions(gi, p.N, lane);
+          if (wr.mode == kModeUmma) {
+            const uint32_t sA = sMask + (uint32_t)mb * kMaskOpBytes, sB = sA + kRow32;
+            for (int r = lane; r < kMaxN; r += 32) {
+              uint32_t a[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u}, b[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+              if (r < p.N) {
+                const uint32_t id = __ldg(gi + r);
+                const int slot = __popc(wr.present & ((1u << id) - 1u));
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  if (slot >> 1 == e) {
+                    a[e] = bias_bits << (16 * (slot & 1));
+                    b[e] = 0x3F80u << (16 * (slot & 1));  // bf16 1.0
+                  }
+                }
+              }
+              const uint32_t sw = (uint32_t)((r >> 2) & 1) << 4;
+              st_shared_v4(sA + r * 32 + sw, a[0], a[1], a[2], a[3]);
+              st_shared_v4(sA + r * 32 + (16u ^ sw), a[4], a[5], a[6], a[7]);
+              st_shared_v4(sB + r * 32 + sw, b[0], b[1], b[2], b[3]);
+              st_shared_v4(sB + r * 32 + (16u ^ sw), b[4], b[5], b[6], b[7]);
+            }
+            fence_proxy_async_shared();
+          }
+          if (lane == 0) mask_mode[mb] = wr.mode;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(BAR(kMaskFull + mb));
+        }
+      }
+      int ok = 1;
+      if (lane == 0) {
         const int s = i % kStages;
         const uint32_t ph = (uint32_t)((i / kStages) & 1);
-        if (!mbar_wait(BAR(empty0 + s), ph ^ 1u, abort, p.status, 11, kTimeoutNs)) break;
-        const int w = t / p.H, h = t - w * p.H;
-        const uint32_t dst = sbase + s * kStageBytes + (qk ? 0u : (uint32_t)kQKBytes);
-        mbar_arrive_expect_tx(BAR(full0 + s), bytes);
-        if (qk) {
-          tma_load_4d(dst, &tmq, BAR(full0 + s), 0, 0, h, w);
-          tma_load_4d(dst + kTileBytes, &tmk, BAR(full0 + s), 0, 0, h, w);
+        if (!mbar_wait(BAR(empty0 + s), ph ^ 1u, abort, p.status, 11, kTimeoutNs)) {
+          ok = 0;
         } else {
-          tma_load_4d(dst, &tmv, BAR(full0 + s), 0, 0, h, w);
+          const uint32_t dst = sbase + s * kStageBytes + (qk ? 0u : (uint32_t)kQKBytes);
+          mbar_arrive_expect_tx(BAR(full0 + s), bytes);
+          if (qk) {
+            tma_load_4d(dst, &tmq, BAR(full0 + s), 0, 0, h, w);
+            tma_load_4d(dst + kTileBytes, &tmk, BAR(full0 + s), 0, 0, h, w);
+          } else {
+            tma_load_4d(dst, &tmv, BAR(full0 + s), 0, 0, h, w);
+          }
+          last_par[s] = (int)ph;
         }
-        last_par[s] = (int)ph;
       }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+    }
+    if (lane == 0) {
       int no_abort = 0;
       for (int s = 0; s < kStages; ++s)
         if (last_par[s] >= 0) mbar_wait(BAR(full0 + s), (uint32_t)last_par[s], &no_abort, p.status, 12, kTimeoutNs);
@@ -634,11 +739,18 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       int ns = 0, npv = 0;
       uint64_t t_last = cycles();
       uint32_t idle = 0;
+      // Window sequence number (within this CTA) of tile ns: selects the mask buffer.
+      int s_wseq = 0;
+      int s_w = t_begin / p.H;
       while (npv < n_local) {
         bool progressed = false;
         if (ns < n_local) {
           const int s = ns % kStages;
-          if (mbar_test_wait(BAR(kFullQK + s), (uint32_t)((ns / kStages) & 1)) &&
+          const int mb = s_wseq & 1;
+          bool mask_ready = true;
+          if constexpr (kMask == kGroups)
+            mask_ready = mbar_test_wait(BAR(kMaskFull + mb), (uint32_t)((s_wseq >> 1) & 1));
+          if (mask_ready && mbar_test_wait(BAR(kFullQK + s), (uint32_t)((ns / kStages) & 1)) &&
               mbar_test_wait(BAR(kSFree), (uint32_t)((ns & 1) ^ 1))) {
             tc_fence_after();
             const uint32_t sQ = sbase + s * kStageBytes, sK = sQ + kTileBytes;
@@ -648,8 +760,26 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
               umma_f16(tmem + kColS, desc_sw128(sQ + k * 32, 16, 1024), b, kIdescS, k > 0 ? 1u : 0u);
               umma_f16(tmem + kColS2, desc_sw128(sQ + kRowOff80 + k * 32, 16, 1024), b, kIdescS2, k > 0 ? 1u : 0u);
             }
+            const int t_next = t_begin + ns + 1;
+            const bool last_of_window = ns + 1 == n_local || t_next / p.H != s_w;
+            if constexpr (kMask == kGroups) {
+              if (mask_mode[mb] == kModeUmma) {
+                // S += onehot(query region) * bias . onehot(key region)^T (one K=16 step).
+                const uint32_t sA = sMask + (uint32_t)mb * kMaskOpBytes, sB = sA + kRow32;
+                const uint64_t b = desc_sw32(sB, 256);
+                umma_f16(tmem + kColS, desc_sw32(sA, 256), b, kIdescS, 1u);
+                umma_f16(tmem + kColS2, desc_sw32(sA + kRowOff80_32, 256), b, kIdescS2, 1u);
+              }
+            }
             umma_commit(BAR(kSFull));
             umma_commit(BAR(kEmptyQK + s));
+            if constexpr (kMask == kGroups) {
+              if (last_of_window) umma_commit(BAR(kMaskEmpty + mb));
+            }
+            if (last_of_window) {
+              ++s_wseq;
+              s_w = t_next / p.H;
+            }
             ++ns;
             progressed = true;
           }
@@ -665,11 +795,17 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
             const uint32_t dO = tmem + (ob ? kColO1 : kColO0);
             const uint32_t dO2 = tmem + kColO2 + (ob ? kLaneHalf : 0u);
 #pragma unroll
-            for (int k = 0; k < 9; ++k) {
+            for (int k = 0; k < 8; ++k) {
               const uint32_t pa = sP + (k >> 2) * kPChunk + (k & 3) * 32;
               const uint64_t b = desc_sw128(sV + k * 2048, kTileBytes, 1024);
               umma_f16(dO, desc_sw128(pa, 16, 1024), b, kIdescO, k > 0 ? 1u : 0u);
               umma_f16(dO2, desc_sw128(pa + kRowOff80, 16, 1024), b, kIdescO2, k > 0 ? 1u : 0u);
+            }
+            {  // keys 128..143: the 32-byte-swizzled P chunk
+              const uint32_t pa = sP + 2 * kPChunk;
+              const uint64_t b = desc_sw128(sV + 8 * 2048, kTileBytes, 1024);
+              umma_f16(dO, desc_sw32(pa, 256), b, kIdescO, 1u);
+              umma_f16(dO2, desc_sw32(pa + kRowOff80_32, 256), b, kIdescO2, 1u);
             }
             umma_commit(BAR(kOFull + ob));
             umma_commit(BAR(kO2Full + ob));
@@ -703,7 +839,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
     const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
     float* xmax = xchg;        // [2][128]
     float* xsum = xchg + 256;  // [2][128]
-    int cached_w = -1;
+    int cached_w = -1, wseq = -1;
     uint32_t rel[3] = {0u, 0u, 0u};
     bool wmask = false;
     float l_prev = 1.f;
@@ -744,9 +880,18 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       if constexpr (kMask != kNoMask) {
         const int w = t / p.H;
         if (w != cached_w) {
-          uint32_t b[5];
-          row_mask_bits<kMask>(p, w % p.nW, row, b);
           cached_w = w;
+          ++wseq;
+          int mode = kModeBits;
+          if constexpr (kMask == kGroups) {
+            // The producer classified the window before its first load (mask buffer wseq & 1).
+            if (!mbar_wait(BAR(kMaskFull + (wseq & 1)), (uint32_t)((wseq >> 1) & 1), abort, p.status, 26,
+                           kTimeoutNs)) { ok = false; break; }
+            mode = mask_mode[wseq & 1];
+          }
+          uint32_t b[5] = {0u, 0u, 0u, 0u, 0u};
+          // Region masks of up to 16 regions are already in S (mask UMMA); others per logit.
+          if (mode == kModeBits) row_mask_bits<kMask>(p, w % p.nW, row, b);
           wmask = (b[0] | b[1] | b[2] | b[3] | b[4]) != 0u;
           // bits of keys 72g .. 72g+71
           const uint32_t w0 = g ? b[2] : b[0], w1 = g ? b[3] : b[1], w2 = g ? b[4] : b[2];
@@ -765,10 +910,8 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kSFree));
       float pm;
-      if (full_n) pm = wmask ? raw_logits72<true, true>(v, rel, braw, 72 * g, p.N)
-                             : raw_logits72<false, true>(v, rel, braw, 72 * g, p.N);
-      else pm = wmask ? raw_logits72<true, false>(v, rel, braw, 72 * g, p.N)
-                      : raw_logits72<false, false>(v, rel, braw, 72 * g, p.N);
+      if (kMask != kNoMask && wmask) pm = raw_logits72<true, kFullN>(v, rel, braw, 72 * g, p.N);
+      else pm = raw_logits72<false, kFullN>(v, rel, braw, 72 * g, p.N);
       // Each slot is rewritten only after the partner passed the other exchange barrier of the
       // same tile, so one slot per value suffices.
       xmax[g * 128 + row] = pm;
@@ -796,7 +939,8 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
 #pragma unroll
       for (int jj = 0; jj < 9; ++jj) {
         const int j16 = 9 * g + jj;  // 8-key group 0..17
-        const uint32_t addr = sP + (j16 >> 3) * kPChunk + row * 128 + (((j16 & 7) ^ (row & 7)) << 4);
+        const uint32_t addr = j16 < 16 ? sP + (j16 >> 3) * kPChunk + row * 128 + (((j16 & 7) ^ (row & 7)) << 4)
+                                       : sP + 2 * kPChunk + sw32_offset(row, (j16 & 1) * 8);
         st_shared_v4(addr, pk[4 * jj], pk[4 * jj + 1], pk[4 * jj + 2], pk[4 * jj + 3]);
       }
       fence_proxy_async_shared();
@@ -813,7 +957,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
     const int t0 = lane & 3, t1 = lane >> 2;
     const int ra = 128 + t1, rb = 136 + t1;
     const uint32_t lane_addr = 96u << 16;  // A rows 48..63 of the M=64 blocks
-    int cached_w = -1;
+    int cached_w = -1, wseq = -1;
     uint32_t ta = 0, tb = 0, kp[18];
     bool wmask = false;
 #pragma unroll
@@ -856,9 +1000,17 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
         const int w = t / p.H;
         if (w != cached_w) {
           cached_w = w;
+          ++wseq;
           const int mw = w % p.nW;
           if constexpr (kMask == kGroups) {
             const uint8_t* gi = p.mask + (int64_t)mw * p.N;
+            // Region masks of up to 16 regions are already in S (mask UMMA); the producer
+            // classified the window before its first load.
+            if (!mbar_wait(BAR(kMaskFull + (wseq & 1)), (uint32_t)((wseq >> 1) & 1), abort, p.status, 27,
+                           kTimeoutNs)) { ok = false; break; }
+            const int mode = mask_mode[wseq & 1];
+            wmask = false;
+            if (mode == kModeBits) {
             ta = ra < p.N ? __ldg(gi + ra) : 0u;
             tb = rb < p.N ? __ldg(gi + rb) : 0u;
             uint32_t any = 0;
@@ -872,6 +1024,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
             }
             // A window with one region has no masked pair; this is uniform over the window.
             wmask = __any_sync(0xffffffffu, any != 0u);
+            }
           } else {
             wmask = true;
           }
@@ -894,32 +1047,51 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kSFree));
       // v[4j + {0,1}] = row ra, keys 8j + 2t0 + {0,1}; v[4j + {2,3}] = row rb, same keys.
+      // The per-logit mask runs in its own loop, behind one warp-uniform branch, so windows whose
+      // mask is already in S (or that have none) execute none of it.
       float mxa = -INFINITY, mxb = -INFINITY;
+      if (kMask != kNoMask && wmask) {
 #pragma unroll
-      for (int j = 0; j < 18; ++j) {
+        for (int j = 0; j < 18; ++j) {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int key = 8 * j + 2 * t0 + e;
-          float ya = __uint_as_float(v[4 * j + e]), yb = __uint_as_float(v[4 * j + 2 + e]);
-          if constexpr (kMask == kGroups) {
-            if (wmask) {
+          for (int e = 0; e < 2; ++e) {
+            const int key = 8 * j + 2 * t0 + e;
+            float ya = __uint_as_float(v[4 * j + e]), yb = __uint_as_float(v[4 * j + 2 + e]);
+            if constexpr (kMask == kGroups) {
               const uint32_t kg = (kp[j] >> (8 * e)) & 0xffu;
               if (kg != ta) ya += braw;
               if (kg != tb) yb += braw;
+            } else if constexpr (kMask == kMaskU8) {
+              const uint8_t* mr = p.mask + (int64_t)(cached_w % p.nW) * p.N * p.N;
+              if (key < p.N && ra < p.N && __ldg(mr + (int64_t)ra * p.N + key)) ya += braw;
+              if (key < p.N && rb < p.N && __ldg(mr + (int64_t)rb * p.N + key)) yb += braw;
             }
-          } else if constexpr (kMask == kMaskU8) {
-            const uint8_t* mr = p.mask + (int64_t)(cached_w % p.nW) * p.N * p.N;
-            if (key < p.N && ra < p.N && __ldg(mr + (int64_t)ra * p.N + key)) ya += braw;
-            if (key < p.N && rb < p.N && __ldg(mr + (int64_t)rb * p.N + key)) yb += braw;
+            if (!kFullN && key >= p.N) {
+              ya = -INFINITY;
+              yb = -INFINITY;
+            }
+            v[4 * j + e] = __float_as_uint(ya);
+            v[4 * j + 2 + e] = __float_as_uint(yb);
+            mxa = fmaxf(mxa, ya);
+            mxb = fmaxf(mxb, yb);
           }
-          if (key >= p.N) {
-            ya = -INFINITY;
-            yb = -INFINITY;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 18; ++j) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int key = 8 * j + 2 * t0 + e;
+            float ya = __uint_as_float(v[4 * j + e]), yb = __uint_as_float(v[4 * j + 2 + e]);
+            if (!kFullN && key >= p.N) {
+              ya = -INFINITY;
+              yb = -INFINITY;
+            }
+            v[4 * j + e] = __float_as_uint(ya);
+            v[4 * j + 2 + e] = __float_as_uint(yb);
+            mxa = fmaxf(mxa, ya);
+            mxb = fmaxf(mxb, yb);
           }
-          v[4 * j + e] = __float_as_uint(ya);
-          v[4 * j + 2 + e] = __float_as_uint(yb);
-          mxa = fmaxf(mxa, ya);
-          mxb = fmaxf(mxb, yb);
         }
       }
       mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
@@ -946,10 +1118,15 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       lb += __shfl_xor_sync(0xffffffffu, lb, 2);
       if (!mbar_wait(BAR(kPEmpty), (uint32_t)((i & 1) ^ 1), abort, p.status, 21, kTimeoutNs)) { ok = false; break; }
 #pragma unroll
-      for (int j = 0; j < 18; ++j) {
+      for (int j = 0; j < 16; ++j) {
         const uint32_t off = (j >> 3) * kPChunk + (uint32_t)(4 * t0);
         st_shared_u32(sP + off + ra * 128 + (((j & 7) ^ (ra & 7)) << 4), pa[j]);
         st_shared_u32(sP + off + rb * 128 + (((j & 7) ^ (rb & 7)) << 4), pb[j]);
+      }
+#pragma unroll
+      for (int j = 16; j < 18; ++j) {  // keys 128..143: the 32-byte-swizzled chunk
+        st_shared_u32(sP + 2 * kPChunk + sw32_offset(ra, (j & 1) * 8 + 2 * t0), pa[j]);
+        st_shared_u32(sP + 2 * kPChunk + sw32_offset(rb, (j & 1) * 8 + 2 * t0), pb[j]);
       }
       fence_proxy_async_shared();
       __syncwarp();
@@ -1010,7 +1187,7 @@ int make_map(CUtensorMap* map, const void* base, bool f32, int64_t Bwin, int64_t
 template <int kMask>
 int launch_tc_bf16(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p,
                    cudaStream_t s) {
-  auto kern = tc::attn_tc_bf16_kernel<kMask>;
+  auto kern = p.N == kMaxN ? tc::attn_tc_bf16_kernel<kMask, true> : tc::attn_tc_bf16_kernel<kMask, false>;
   FA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmem));
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
   kern<<<grid, tc::kThreads, tc::kSmem, s>>>(mq, mk, mv, p);

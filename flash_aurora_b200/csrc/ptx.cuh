@@ -236,6 +236,18 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo, uin
   return d;
 }
 
+// Same for a K-major tile in the 32-byte swizzle (rows of 32 bytes = 16 bf16, 8-row atoms of 256
+// bytes, 16-byte chunk index XOR address bit 7); the K extent of one UMMA fits one row, so only
+// the 8-row group stride (sbo) matters.
+__device__ __forceinline__ uint64_t desc_sw32(uint32_t saddr, uint32_t sbo) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;  // leading byte offset: unused for this layout
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)6 << 61;  // SWIZZLE_32B
+  return d;
+}
+
 // Instruction descriptor: fp32 accumulate, A/B format (0 f16, 1 bf16, 2 tf32), majors, M x N.
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_format, int M, int N, bool a_mn_major, bool b_mn_major) {
   return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((a_mn_major ? 1u : 0u) << 15) |
