@@ -455,8 +455,10 @@ def run_layout_adaln(args) -> None:
     ]
     # The MLP activation at stage 1 of config 4: fc1 output (259200, 2048) bf16, in place.
     h = torch.randn(259200, 2048, device=dev, generator=g).bfloat16()
-    cases.append(("mlp exact GELU, S1 fc1 output (259200, 2048) bf16, in place",
+    cases.append(("mlp exact GELU (erfc form), S1 fc1 output (259200, 2048) bf16, in place",
                   lambda: fa.gelu_erf(h, inplace=True), h.numel() * 2 * 2))
+    cases.append(("mlp exact GELU (erff, PyTorch arithmetic), same tensor",
+                  lambda: fa.gelu_erf(h, inplace=True, method="erff"), h.numel() * 2 * 2))
     cases.append(("[torch F.gelu on the same tensor, for comparison]",
                   lambda: torch.nn.functional.gelu(h), h.numel() * 2 * 2))
     for name, fn, nbytes in cases:

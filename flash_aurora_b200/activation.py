@@ -1,8 +1,11 @@
 """Exact (erf) GELU of the block MLP on the CUDA library (``fa_gelu_erf``).
 
 Upstream applies ``nn.GELU()`` between fc1 and fc2 (``aurora/model/swin3d.py:73-109``). Here it
-runs in place on the bf16 fc1 output with 16-byte streaming accesses; the arithmetic is PyTorch's
-(``x * 0.5 * (1 + erf(x / sqrt(2)))`` in fp32, rounded to the tensor dtype).
+runs in place on the bf16 fc1 output with 16-byte streaming accesses. ``method="erff"`` is
+PyTorch's arithmetic (``x * 0.5 * (1 + erff(x / sqrt(2)))`` in fp32), bit-identical to
+``F.gelu``; ``method="poly"`` (the block's default) evaluates Phi from a fitted erfc form on paired
+fp32 FMAs, about 1.5x cheaper, and rounds to the exact GELU for every bf16 input with |x| < 4
+(|GELU| < 1.3e-4 beyond, within 1e-6).
 """
 
 from __future__ import annotations
@@ -16,10 +19,16 @@ from . import _lib
 __all__ = ["gelu_erf"]
 
 
-def gelu_erf(x: torch.Tensor, out: Optional[torch.Tensor] = None, *, inplace: bool = False) -> torch.Tensor:
+_METHODS = {"erff": _lib.FA_GELU_ERFF, "poly": _lib.FA_GELU_POLY}
+
+
+def gelu_erf(x: torch.Tensor, out: Optional[torch.Tensor] = None, *, inplace: bool = False,
+             method: str = "poly") -> torch.Tensor:
     """``GELU(x)`` for a CUDA float32/bfloat16 tensor; ``inplace=True`` overwrites ``x``."""
     if x.device.type != "cuda" or x.dtype not in (torch.float32, torch.bfloat16):
         raise ValueError("gelu_erf requires a CUDA float32/bfloat16 tensor.")
+    if method not in _METHODS:
+        raise ValueError(f"method must be one of {tuple(_METHODS)}")
     if inplace:
         if not x.is_contiguous():
             raise ValueError("in-place gelu_erf needs a contiguous tensor")
@@ -31,6 +40,6 @@ def gelu_erf(x: torch.Tensor, out: Optional[torch.Tensor] = None, *, inplace: bo
         elif out.shape != x.shape or out.dtype != x.dtype or not out.is_contiguous() or out.device != x.device:
             raise ValueError("out must be a contiguous tensor of x's shape, dtype and device")
     rc = _lib.load().fa_gelu_erf(x.data_ptr(), out.data_ptr(), _lib.dtype_code(x.dtype), x.numel(),
-                                 _lib.stream_ptr(x.device))
+                                 _METHODS[method], _lib.stream_ptr(x.device))
     _lib.check(rc, "gelu_erf")
     return out

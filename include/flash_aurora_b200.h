@@ -143,12 +143,16 @@ int fa_unmerge_adaln_film_band(const void* windows, const void* halo_in, int win
                                void* stream);
 
 /*
- * Exact GELU, out[i] = x[i] * 0.5 * (1 + erf(x[i] / sqrt(2))) in fp32, rounded to dtype
- * (FA_F32 | FA_BF16); n elements, contiguous; out == x (in place) is allowed, any other overlap is
- * rejected. Replaces the nn.GELU() between fc1 and fc2 of the block MLP (swin3d.py:73-109), which
- * upstream runs as a PyTorch elementwise kernel.
+ * Exact GELU, out[i] = x[i] * Phi(x[i]) = x[i] * 0.5 * (1 + erf(x[i] / sqrt(2))) in fp32, rounded to
+ * dtype (FA_F32 | FA_BF16); n elements, contiguous; out == x (in place) is allowed, any other
+ * overlap is rejected. Replaces the nn.GELU() between fc1 and fc2 of the block MLP
+ * (swin3d.py:73-109), which upstream runs as a PyTorch elementwise kernel.
+ * method FA_GELU_ERFF: PyTorch's arithmetic (erff), bit-identical to it.
+ * method FA_GELU_POLY: Phi from a fitted erfc form without the 1 + erf cancellation, about 1.5x
+ * cheaper; bf16 results equal the correctly rounded GELU for |x| < 4.
  */
-int fa_gelu_erf(const void* x, void* out, int dtype, int64_t n, void* stream);
+enum { FA_GELU_ERFF = 0, FA_GELU_POLY = 1 };
+int fa_gelu_erf(const void* x, void* out, int dtype, int64_t n, int method, void* stream);
 
 /*
  * Shifted-window region ids of every window token, (nW, N) uint8 written to HOST memory.
