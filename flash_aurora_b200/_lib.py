@@ -21,8 +21,10 @@ FA_OK, FA_ERR_INVALID, FA_ERR_UNSUPPORTED, FA_ERR_CUDA, FA_ERR_TIMEOUT = 0, -1, 
 FA_ATTN_BF16, FA_ATTN_FP32_3XTF32 = 0, 1
 FA_LAYOUT_BHND, FA_LAYOUT_BNC = 0, 1
 FA_GELU_ERFF, FA_GELU_POLY = 0, 1
+FA_ATTN_FLAG_REGIONS_FIT = 1
 
 _i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p
+_u32 = ctypes.c_uint
 _i32p = ctypes.POINTER(ctypes.c_int32)
 _i64p = ctypes.POINTER(ctypes.c_int64)
 _u8p = ctypes.c_void_p
@@ -46,8 +48,10 @@ SIGNATURES = {
                                           _i64, _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
     "fa_gelu_erf": (_i32, [_vp, _vp, _i32, _i64, _i32, _vp]),
     "fa_shifted_window_groups": (_i32, [_i64, _i64, _i64, _i32p, _i32p, _i32, _u8p]),
-    "fa_window_attention": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64p, _u8p, _u8p, _i64, _f32, _vp]),
-    "fa_window_attention_qkvpacked": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _u8p, _u8p, _i64, _f32, _vp]),
+    "fa_window_attention": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64p, _u8p, _u8p, _i64, _f32,
+                                   _u32, _vp]),
+    "fa_window_attention_qkvpacked": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _u8p, _u8p, _i64, _f32,
+                                             _u32, _vp]),
     "fa_window_attention_bias_noalloc": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64p, _vp,
                                                  _i64, _f32, _vp]),
     "fa_attention_status": (_i32, [ctypes.POINTER(ctypes.c_int)]),

@@ -499,6 +499,57 @@ __device__ __forceinline__ WindowRegions window_regions(const uint8_t* gi, int N
   return r;
 }
 
+// Region-id masks (built into the mask UMMA) and masks with a per-logit path.
+template <int kMask> constexpr bool kRegions = kMask == kGroups || kMask == kGroupsFit;
+template <int kMask> constexpr bool kBitsPath = kMask == kGroups || kMask == kMaskU8;
+
+// Region ids of the tokens k = lane + 32 m (m < 5) of one window; 0xFF past N.
+__device__ __forceinline__ void load_window_ids(const uint8_t* gi, int N, int lane, uint32_t (&ids)[5]) {
+#pragma unroll
+  for (int m = 0; m < 5; ++m) {
+    const int k = lane + 32 * m;
+    ids[m] = k < N ? (uint32_t)__ldg(gi + k) : 0xFFu;
+  }
+}
+
+// Mode of a window from ids held by the 32 lanes (same rule as window_regions).
+__device__ __forceinline__ WindowRegions regions_from_ids(const uint32_t (&ids)[5]) {
+  uint32_t pres = 0u, over = 0u;
+#pragma unroll
+  for (int m = 0; m < 5; ++m) {
+    if (ids[m] == 0xFFu) continue;
+    if (ids[m] < 32u) pres |= 1u << ids[m]; else over = 1u;
+  }
+  pres = __reduce_or_sync(0xffffffffu, pres);
+  over = __reduce_or_sync(0xffffffffu, over);
+  const int distinct = __popc(pres);
+  WindowRegions r;
+  r.present = pres;
+  r.mode = over || distinct > 16 ? kModeBits : (distinct > 1 ? kModeUmma : kModeNone);
+  return r;
+}
+
+// One 32-byte row of a one-hot operand: `value` (bf16 bits) at element `slot`, zeros elsewhere;
+// slot >= 16 writes a zero row.
+__device__ __forceinline__ void store_onehot_row(uint32_t tile, int r, int slot, uint32_t value) {
+  const uint32_t swz = (uint32_t)((r >> 2) & 1);
+  const uint32_t v = value << (16 * (slot & 1));
+  const int wi = (slot >> 1) & 3;
+  const uint32_t hot = slot < 16 ? (uint32_t)(slot >> 3) : 2u;  // chunk holding the element
+  const uint32_t x0 = wi == 0 ? v : 0u, x1 = wi == 1 ? v : 0u, x2 = wi == 2 ? v : 0u, x3 = wi == 3 ? v : 0u;
+  const uint32_t row = tile + (uint32_t)r * 32u;
+  if (hot == 0u) {
+    st_shared_v4(row + ((0u ^ swz) << 4), x0, x1, x2, x3);
+    st_shared_v4(row + ((1u ^ swz) << 4), 0u, 0u, 0u, 0u);
+  } else if (hot == 1u) {
+    st_shared_v4(row + ((0u ^ swz) << 4), 0u, 0u, 0u, 0u);
+    st_shared_v4(row + ((1u ^ swz) << 4), x0, x1, x2, x3);
+  } else {
+    st_shared_v4(row, 0u, 0u, 0u, 0u);
+    st_shared_v4(row + 16u, 0u, 0u, 0u, 0u);
+  }
+}
+
 __device__ __forceinline__ uint32_t nibble_of_bytes(uint32_t ne) {
   return (ne & 1u) | ((ne >> 7) & 2u) | ((ne >> 14) & 4u) | ((ne >> 21) & 8u);
 }
@@ -666,40 +717,46 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
     int cur_w = -1, wseq = -1;
     // The mask bias of same-region pairs in the raw logit domain, as a bf16 operand value.
     const uint32_t bias_bits = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(-braw));
+    // Region ids of the next window, loaded one window ahead so that classifying a window and
+    // writing its operands waits on no memory.
+    uint32_t nids[5] = {0xFFu, 0xFFu, 0xFFu, 0xFFu, 0xFFu};
+    if constexpr (kRegions<kMask>) {
+      if (qk && n_local > 0) load_window_ids(p.mask + (int64_t)((t_begin / p.H) % p.nW) * p.N, p.N, lane, nids);
+    }
     for (int i = 0; i < n_local; ++i) {
       const int t = t_begin + i;
       const int w = t / p.H, h = t - w * p.H;
-      if constexpr (kMask == kGroups) {
+      if constexpr (kRegions<kMask>) {
         if (qk && w != cur_w) {
           cur_w = w;
           ++wseq;
           const int mb = wseq & 1;
           const uint32_t u = (uint32_t)(wseq >> 1);
+          uint32_t ids[5];
+#pragma unroll
+          for (int m = 0; m < 5; ++m) ids[m] = nids[m];
+          if ((w + 1) * p.H < t_begin + n_local)
+            load_window_ids(p.mask + (int64_t)((w + 1) % p.nW) * p.N, p.N, lane, nids);
+          WindowRegions wr = regions_from_ids(ids);
+          if constexpr (kMask == kGroupsFit) {
+            if (wr.mode == kModeBits) {  // the caller's promise does not hold: report, leave unmasked
+              if (lane == 0) atomicCAS(p.status, 0, 28);
+              wr.mode = kModeNone;
+            }
+          }
           int okw = 1;
           if (lane == 0) okw = mbar_wait(BAR(kMaskEmpty + mb), (u & 1u) ^ 1u, abort, p.status, 13, kTimeoutNs);
           if (!__shfl_sync(0xffffffffu, okw, 0)) break;
-          const uint8_t* gi = p.mask + (int64_t)(w % p.nW) * p.N;
-          const WindowRegions wr = window_regions(gi, p.N, lane);
           if (wr.mode == kModeUmma) {
             const uint32_t sA = sMask + (uint32_t)mb * kMaskOpBytes, sB = sA + kRow32;
-            for (int r = lane; r < kMaxN; r += 32) {
-              uint32_t a[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u}, b[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-              if (r < p.N) {
-                const uint32_t id = __ldg(gi + r);
-                const int slot = __popc(wr.present & ((1u << id) - 1u));
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                  if (slot >> 1 == e) {
-                    a[e] = bias_bits << (16 * (slot & 1));
-                    b[e] = 0x3F80u << (16 * (slot & 1));  // bf16 1.0
-                  }
-                }
+            for (int m = 0; m < 5; ++m) {
+              const int r = lane + 32 * m;
+              if (r < kMaxN) {
+                const int slot = ids[m] < 32u ? __popc(wr.present & ((1u << ids[m]) - 1u)) : 16;
+                store_onehot_row(sA, r, slot, bias_bits);
+                store_onehot_row(sB, r, slot, 0x3F80u);  // bf16 1.0
               }
-              const uint32_t sw = (uint32_t)((r >> 2) & 1) << 4;
-              st_shared_v4(sA + r * 32 + sw, a[0], a[1], a[2], a[3]);
-              st_shared_v4(sA + r * 32 + (16u ^ sw), a[4], a[5], a[6], a[7]);
-              st_shared_v4(sB + r * 32 + sw, b[0], b[1], b[2], b[3]);
-              st_shared_v4(sB + r * 32 + (16u ^ sw), b[4], b[5], b[6], b[7]);
             }
             fence_proxy_async_shared();
           }
@@ -748,7 +805,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
           const int s = ns % kStages;
           const int mb = s_wseq & 1;
           bool mask_ready = true;
-          if constexpr (kMask == kGroups)
+          if constexpr (kRegions<kMask>)
             mask_ready = mbar_test_wait(BAR(kMaskFull + mb), (uint32_t)((s_wseq >> 1) & 1));
           if (mask_ready && mbar_test_wait(BAR(kFullQK + s), (uint32_t)((ns / kStages) & 1)) &&
               mbar_test_wait(BAR(kSFree), (uint32_t)((ns & 1) ^ 1))) {
@@ -762,7 +819,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
             }
             const int t_next = t_begin + ns + 1;
             const bool last_of_window = ns + 1 == n_local || t_next / p.H != s_w;
-            if constexpr (kMask == kGroups) {
+            if constexpr (kRegions<kMask>) {
               if (mask_mode[mb] == kModeUmma) {
                 // S += onehot(query region) * bias . onehot(key region)^T (one K=16 step).
                 const uint32_t sA = sMask + (uint32_t)mb * kMaskOpBytes, sB = sA + kRow32;
@@ -773,7 +830,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
             }
             umma_commit(BAR(kSFull));
             umma_commit(BAR(kEmptyQK + s));
-            if constexpr (kMask == kGroups) {
+            if constexpr (kRegions<kMask>) {
               if (last_of_window) umma_commit(BAR(kMaskEmpty + mb));
             }
             if (last_of_window) {
@@ -883,7 +940,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
           cached_w = w;
           ++wseq;
           int mode = kModeBits;
-          if constexpr (kMask == kGroups) {
+          if constexpr (kRegions<kMask>) {
             // The producer classified the window before its first load (mask buffer wseq & 1).
             if (!mbar_wait(BAR(kMaskFull + (wseq & 1)), (uint32_t)((wseq >> 1) & 1), abort, p.status, 26,
                            kTimeoutNs)) { ok = false; break; }
@@ -891,7 +948,9 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
           }
           uint32_t b[5] = {0u, 0u, 0u, 0u, 0u};
           // Region masks of up to 16 regions are already in S (mask UMMA); others per logit.
-          if (mode == kModeBits) row_mask_bits<kMask>(p, w % p.nW, row, b);
+          if constexpr (kBitsPath<kMask>) {
+            if (mode == kModeBits) row_mask_bits<kMask>(p, w % p.nW, row, b);
+          }
           wmask = (b[0] | b[1] | b[2] | b[3] | b[4]) != 0u;
           // bits of keys 72g .. 72g+71
           const uint32_t w0 = g ? b[2] : b[0], w1 = g ? b[3] : b[1], w2 = g ? b[4] : b[2];
@@ -910,7 +969,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kSFree));
       float pm;
-      if (kMask != kNoMask && wmask) pm = raw_logits72<true, kFullN>(v, rel, braw, 72 * g, p.N);
+      if (kBitsPath<kMask> && wmask) pm = raw_logits72<kBitsPath<kMask>, kFullN>(v, rel, braw, 72 * g, p.N);
       else pm = raw_logits72<false, kFullN>(v, rel, braw, 72 * g, p.N);
       // Each slot is rewritten only after the partner passed the other exchange barrier of the
       // same tile, so one slot per value suffices.
@@ -1002,7 +1061,13 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
           cached_w = w;
           ++wseq;
           const int mw = w % p.nW;
-          if constexpr (kMask == kGroups) {
+          if constexpr (kMask == kGroupsFit) {
+            // The mask is in S (mask UMMA); only wait for the producer's classification so
+            // that this warp follows the same window sequence.
+            if (!mbar_wait(BAR(kMaskFull + (wseq & 1)), (uint32_t)((wseq >> 1) & 1), abort, p.status, 27,
+                           kTimeoutNs)) { ok = false; break; }
+            wmask = false;
+          } else if constexpr (kMask == kGroups) {
             const uint8_t* gi = p.mask + (int64_t)mw * p.N;
             // Region masks of up to 16 regions are already in S (mask UMMA); the producer
             // classified the window before its first load.
@@ -1050,7 +1115,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       // The per-logit mask runs in its own loop, behind one warp-uniform branch, so windows whose
       // mask is already in S (or that have none) execute none of it.
       float mxa = -INFINITY, mxb = -INFINITY;
-      if (kMask != kNoMask && wmask) {
+      if (kBitsPath<kMask> && wmask) {
 #pragma unroll
         for (int j = 0; j < 18; ++j) {
 #pragma unroll
@@ -1222,9 +1287,10 @@ int* status_ptr() {
 
 int run(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const void* q, const void* k,
         const void* v, void* out, const int64_t* strides, const uint8_t* mask_u8,
-        const uint8_t* group_ids, int64_t nW, float scale, void* stream) {
+        const uint8_t* group_ids, int64_t nW, float scale, unsigned flags, void* stream) {
   FA_REQUIRE(precision == FA_ATTN_BF16 || precision == FA_ATTN_FP32_3XTF32, FA_ERR_INVALID,
              "precision must be FA_ATTN_BF16 or FA_ATTN_FP32_3XTF32");
+  FA_REQUIRE((flags & ~(unsigned)FA_ATTN_FLAG_REGIONS_FIT) == 0, FA_ERR_INVALID, "unknown attention flags");
   FA_REQUIRE(strides, FA_ERR_INVALID, "null stride pointer");
   FA_REQUIRE(Bwin >= 0 && H >= 1 && N >= 1, FA_ERR_INVALID, "invalid attention shape");
   FA_REQUIRE((q && k && v && out) || Bwin == 0, FA_ERR_INVALID, "null tensor pointer");
@@ -1274,7 +1340,10 @@ int run(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const voi
     if (kind == kMaskU8) return launch_sync<false, kMaskU8>(mq, mk, mv, p, s);
     return launch_sync<false, kNoMask>(mq, mk, mv, p, s);
   }
-  if (kind == kGroups) return launch_tc_bf16<kGroups>(mq, mk, mv, p, s);
+  if (kind == kGroups) {
+    if (flags & FA_ATTN_FLAG_REGIONS_FIT) return launch_tc_bf16<kGroupsFit>(mq, mk, mv, p, s);
+    return launch_tc_bf16<kGroups>(mq, mk, mv, p, s);
+  }
   if (kind == kMaskU8) return launch_tc_bf16<kMaskU8>(mq, mk, mv, p, s);
   return launch_tc_bf16<kNoMask>(mq, mk, mv, p, s);
 }
@@ -1287,14 +1356,16 @@ using namespace fa;
 extern "C" int fa_window_attention(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh,
                                    const void* q, const void* k, const void* v, void* out,
                                    const int64_t strides[12], const uint8_t* mask_u8,
-                                   const uint8_t* group_ids, int64_t nW, float scale, void* stream) {
-  return attn::run(precision, Bwin, H, N, Dh, q, k, v, out, strides, mask_u8, group_ids, nW, scale, stream);
+                                   const uint8_t* group_ids, int64_t nW, float scale, unsigned flags,
+                                   void* stream) {
+  return attn::run(precision, Bwin, H, N, Dh, q, k, v, out, strides, mask_u8, group_ids, nW, scale, flags,
+                   stream);
 }
 
 extern "C" int fa_window_attention_qkvpacked(int precision, int64_t Bwin, int64_t N, int64_t H,
                                              int64_t Dh, const void* qkv, void* out, int out_layout,
                                              const uint8_t* mask_u8, const uint8_t* group_ids,
-                                             int64_t nW, float scale, void* stream) {
+                                             int64_t nW, float scale, unsigned flags, void* stream) {
   FA_REQUIRE((qkv && out) || Bwin == 0, FA_ERR_INVALID, "null tensor pointer");
   FA_REQUIRE(out_layout == FA_LAYOUT_BHND || out_layout == FA_LAYOUT_BNC, FA_ERR_INVALID,
              "out_layout must be FA_LAYOUT_BHND or FA_LAYOUT_BNC");
@@ -1308,7 +1379,7 @@ extern "C" int fa_window_attention_qkvpacked(int precision, int64_t Bwin, int64_
   else { st[9] = H * N * Dh; st[10] = N * Dh; st[11] = Dh; }
   const char* base = reinterpret_cast<const char*>(qkv);
   return attn::run(precision, Bwin, H, N, Dh, base, base + C * es, base + 2 * C * es, out, st, mask_u8,
-                   group_ids, nW, scale, stream);
+                   group_ids, nW, scale, flags, stream);
 }
 
 extern "C" int fa_attention_status(int* status_out) {

@@ -11,7 +11,10 @@ constexpr int kTileBytes = kMaxN * 128;      // one 144-row tile of 128-byte row
 constexpr uint64_t kTimeoutNs = 2000000000;  // bound of every device-side wait (2 s)
 constexpr float kMaskedLog2 = -144.26950408889634f;  // -100 * log2(e): masked logit bias
 
-enum MaskKind { kNoMask = 0, kGroups = 1, kMaskU8 = 2 };
+// kGroups: (nW, N) region ids of any form; kGroupsFit: region ids the caller guarantees to have at
+// most 16 distinct values below 32 per window (the shifted-window masks do), which lets the bf16
+// tensor-core kernel drop its per-logit fallback; kMaskU8: an (nW, N, N) byte mask.
+enum MaskKind { kNoMask = 0, kGroups = 1, kMaskU8 = 2, kGroupsFit = 3 };
 
 struct Params {
   int Bwin, H, N, nW;
@@ -30,7 +33,7 @@ int* status_ptr();
 // kernels in attention.cu; allocates nothing.
 int run(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const void* q, const void* k,
         const void* v, void* out, const int64_t* strides, const uint8_t* mask_u8, const uint8_t* group_ids,
-        int64_t nW, float scale, void* stream);
+        int64_t nW, float scale, unsigned flags, void* stream);
 
 }  // namespace attn
 }  // namespace fa

@@ -72,5 +72,5 @@ extern "C" int fa_window_attention_bias_noalloc(int precision, int64_t Bwin, int
   pack_bias_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(bias, mask, mask_bytes);
   rc = check_launch("pack_bias_kernel");
   if (rc != FA_OK) return rc;
-  return attn::run(precision, Bwin, H, N, Dh, q, k, v, out, strides, mask, nullptr, nW, scale, stream);
+  return attn::run(precision, Bwin, H, N, Dh, q, k, v, out, strides, mask, nullptr, nW, scale, 0u, stream);
 }

@@ -132,7 +132,7 @@ class BandContext:
 
     def group_ids(self, window_size, shift_size, warped: bool, device) -> Optional[torch.Tensor]:
         """The band's ``(nW_band, N)`` region ids, or ``None`` for an unshifted block."""
-        from .window_attn import shifted_window_group_ids
+        from .window_attn import mark_region_ids_fit, shifted_window_group_ids
 
         ws, ss = maybe_adjust_windows(tuple(window_size), tuple(shift_size), self.field_res)
         if not any(ss):
@@ -145,6 +145,8 @@ class BandContext:
             g1 = [-(-d // w) for d, w in zip((C, H, W), ws)]
             a, b = self.h_begin // ws[1], self.h_end // ws[1]
             hit = full.view(g1[0], g1[1], g1[2], -1)[:, a:b].reshape(-1, full.shape[-1]).contiguous()
+            # The band's windows are a subset of the field's: the field's tensor-core fit carries over.
+            mark_region_ids_fit(hit, getattr(full, "_fa_regions_fit", False))
             self._gids[key] = hit
         return hit
 

@@ -107,6 +107,27 @@ def _group_ids_host(res, window_size, shift_size, warped):
 
 
 _GROUP_CACHE: dict = {}
+# Attribute set on region-id tensors known to fit the tensor-core mask: every window has at most
+# 16 distinct ids, all below 32 (FA_ATTN_FLAG_REGIONS_FIT).
+_REGIONS_FIT = "_fa_regions_fit"
+
+
+def region_ids_fit(ids: np.ndarray) -> bool:
+    """True when every window (row) of ``ids`` has at most 16 distinct values, all below 32."""
+    ids = np.asarray(ids)
+    if ids.size == 0:
+        return True
+    if int(ids.max()) >= 32:
+        return False
+    present = np.zeros((ids.shape[0], 32), dtype=bool)
+    present[np.arange(ids.shape[0])[:, None], ids.astype(np.int64)] = True
+    return bool((present.sum(axis=1) <= 16).all())
+
+
+def mark_region_ids_fit(t: torch.Tensor, fits: bool = True) -> torch.Tensor:
+    """Record on ``t`` that its region ids fit the tensor-core mask (see :func:`region_ids_fit`)."""
+    setattr(t, _REGIONS_FIT, bool(fits))
+    return t
 
 
 def shifted_window_group_ids(res, window_size, shift_size, warped: bool = True,
@@ -115,10 +136,18 @@ def shifted_window_group_ids(res, window_size, shift_size, warped: bool = True,
     key = (tuple(res), tuple(window_size), tuple(shift_size), bool(warped), str(device))
     t = _GROUP_CACHE.get(key)
     if t is None:
-        host = torch.from_numpy(_group_ids_host(tuple(res), tuple(window_size), tuple(shift_size), bool(warped)).copy())
+        arr = _group_ids_host(tuple(res), tuple(window_size), tuple(shift_size), bool(warped))
+        host = torch.from_numpy(arr.copy())
         t = host.to(device) if device is not None else host
+        mark_region_ids_fit(t, region_ids_fit(arr))
         _GROUP_CACHE[key] = t
     return t
+
+
+def _attn_flags(group_ids: Optional[torch.Tensor]) -> int:
+    if group_ids is not None and getattr(group_ids, _REGIONS_FIT, False):
+        return _lib.FA_ATTN_FLAG_REGIONS_FIT
+    return 0
 
 
 def _precision_code(precision: WinAttnPrecision) -> int:
@@ -178,7 +207,8 @@ def window_attn_fwd_cute(
     rc = _lib.load().fa_window_attention(
         _precision_code(precision), Bwin, H, N, Dh, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
         strides, mask_u8.data_ptr() if mask_u8 is not None else None,
-        gids.data_ptr() if gids is not None else None, nW, float(scale_qk), _lib.stream_ptr(q.device))
+        gids.data_ptr() if gids is not None else None, nW, float(scale_qk), _attn_flags(group_ids),
+        _lib.stream_ptr(q.device))
     _lib.check(rc, "window_attn_fwd_cute")
     del keep
     return out
@@ -226,7 +256,7 @@ def window_attn_fwd_cute_qkvpacked(
     rc = _lib.load().fa_window_attention_qkvpacked(
         prec, Bwin, N, H, Dh, qkv.data_ptr(), out.data_ptr(), layout,
         mask_u8.data_ptr() if mask_u8 is not None else None, gids.data_ptr() if gids is not None else None,
-        nW, float(scale_qk), _lib.stream_ptr(qkv.device))
+        nW, float(scale_qk), _attn_flags(group_ids), _lib.stream_ptr(qkv.device))
     _lib.check(rc, "window_attn_fwd_cute_qkvpacked")
     _record_end(ev0, Bwin, H, N, Dh, qkv.element_size())
     del keep

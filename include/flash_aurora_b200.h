@@ -37,6 +37,8 @@ enum {
   FA_ATTN_FP32_3XTF32 = 1  /* fp32 in/out, 3xTF32 split products, fp32 softmax */
 };
 
+enum { FA_ATTN_FLAG_REGIONS_FIT = 1 };
+
 /* Attention output layouts (upstream output_layout "bhnd" / "bnc", window_attn_fwd.py:246-255). */
 enum { FA_LAYOUT_BHND = 0, FA_LAYOUT_BNC = 1 };
 
@@ -171,12 +173,17 @@ int fa_shifted_window_groups(int64_t C, int64_t H, int64_t W, const int32_t wind
  * ids differ; window b uses mask index b % nW. A masked logit gets -100 added after scaling
  * (upstream bias semantics, swin3d.py:597; CuTe kernel ops/cute/_kernel_bf16.py:361-365).
  * Supported: Dh == 64, 1 <= N <= 144 for FA_ATTN_BF16 and FA_ATTN_FP32_3XTF32.
+ * flags: 0, or FA_ATTN_FLAG_REGIONS_FIT when every window of group_ids has at most 16 distinct ids,
+ * all below 32 (true of the shifted-window ids of fa_shifted_window_groups); the bf16 kernel then
+ * runs without its per-logit mask path. A window breaking that promise is left unmasked and
+ * fa_attention_status reports 28.
  * Replaces window_attn_fwd_cute (ops/cute/window_attn_fwd.py:141-243).
  */
 int fa_window_attention(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh,
                         const void* q, const void* k, const void* v, void* out,
                         const int64_t strides[12], const uint8_t* mask_u8,
-                        const uint8_t* group_ids, int64_t nW, float scale, void* stream);
+                        const uint8_t* group_ids, int64_t nW, float scale, unsigned flags,
+                        void* stream);
 
 /*
  * Same on the packed output of Linear(D, 3D): qkv (Bwin, N, 3, H, Dh) contiguous; out is
@@ -186,7 +193,7 @@ int fa_window_attention(int precision, int64_t Bwin, int64_t H, int64_t N, int64
 int fa_window_attention_qkvpacked(int precision, int64_t Bwin, int64_t N, int64_t H, int64_t Dh,
                                   const void* qkv, void* out, int out_layout,
                                   const uint8_t* mask_u8, const uint8_t* group_ids, int64_t nW,
-                                  float scale, void* stream);
+                                  float scale, unsigned flags, void* stream);
 
 /*
  * fa_window_attention with a float bias (nW, N, N) (bias < -50 means masked, as upstream) that

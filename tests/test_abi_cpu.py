@@ -78,11 +78,11 @@ def test_invalid_arguments_return_status_without_a_gpu(lib):
     assert rc == _lib.FA_ERR_INVALID
     strides = (ctypes.c_int64 * 12)(*([64] * 12))
     p = ctypes.c_void_p(1 << 20)
-    rc = lib.fa_window_attention(0, 4, 8, 144, 32, p, p, p, p, strides, None, None, 0, 0.125, None)
+    rc = lib.fa_window_attention(0, 4, 8, 144, 32, p, p, p, p, strides, None, None, 0, 0.125, 0, None)
     assert rc == _lib.FA_ERR_UNSUPPORTED and b"head_dim" in lib.fa_last_error()
-    rc = lib.fa_window_attention(0, 4, 8, 288, 64, p, p, p, p, strides, None, None, 0, 0.125, None)
+    rc = lib.fa_window_attention(0, 4, 8, 288, 64, p, p, p, p, strides, None, None, 0, 0.125, 0, None)
     assert rc == _lib.FA_ERR_UNSUPPORTED
-    rc = lib.fa_window_attention(5, 4, 8, 144, 64, p, p, p, p, strides, None, None, 0, 0.125, None)
+    rc = lib.fa_window_attention(5, 4, 8, 144, 64, p, p, p, p, strides, None, None, 0, 0.125, 0, None)
     assert rc == _lib.FA_ERR_INVALID
     rc = lib.fa_adaln_film(p, 0, None, 0, p, p, 0, 0.0, 1e-5, p, 0, None, 1, 4, 4096, None)
     assert rc == _lib.FA_ERR_UNSUPPORTED and b"2048" in lib.fa_last_error()
@@ -114,3 +114,20 @@ def test_band_arguments_return_status_without_a_gpu(lib):
     # an unshifted band needs no halo and nothing is extracted (no launch, so no GPU needed)
     z = _lib.i32x3((0, 0, 0))
     assert lib.fa_band_halo_extract(p, 0, p, 0, 1, 4, 12, 36, 72, 64, ws, z, None) == _lib.FA_OK
+
+
+def test_attention_flags_validated_without_a_gpu(lib):
+    from flash_aurora_b200 import _lib
+    strides = (ctypes.c_int64 * 12)(*([64] * 12))
+    p = ctypes.c_void_p(1 << 20)
+    rc = lib.fa_window_attention(0, 4, 8, 144, 64, p, p, p, p, strides, None, None, 0, 0.125, 6, None)
+    assert rc == _lib.FA_ERR_INVALID and b"flags" in lib.fa_last_error()
+
+
+def test_region_ids_fit_rule():
+    from flash_aurora_b200.window_attn import region_ids_fit
+    assert region_ids_fit(OL.window_group_ids((4, 36, 72), (2, 6, 12), (1, 3, 6)))
+    assert region_ids_fit(OL.window_group_ids((4, 45, 90), (2, 6, 12), (1, 3, 6)))
+    assert region_ids_fit(np.tile(np.arange(16, dtype=np.uint8), (3, 9)))
+    assert not region_ids_fit(np.tile(np.arange(17, dtype=np.uint8), (2, 1)))
+    assert not region_ids_fit(np.full((2, 144), 40, dtype=np.uint8))

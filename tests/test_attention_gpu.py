@@ -207,3 +207,31 @@ def test_region_id_patterns_all_mask_modes(H):
     for w in range(Bwin):
         assert _rel_l2(a[w], ref[w]) <= 1e-2, w
     assert (a.float() - b.float()).abs().max().item() <= 2e-2
+
+
+def test_region_fit_flag_fast_path_and_broken_promise():
+    """Region ids tagged as fitting the tensor-core mask run the kernel without the per-logit
+    path; a tagged tensor that breaks the promise is reported through the status word (28)."""
+    import ctypes
+
+    from flash_aurora_b200 import _lib
+    from flash_aurora_b200.window_attn import mark_region_ids_fit, region_ids_fit
+
+    N, nW, H = 144, 4, 4
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(0, 6, (nW, N), generator=g).to(torch.uint8)
+    assert region_ids_fit(ids.numpy())
+    q, k, v = (t.bfloat16().cuda() for t in _qkv(2 * nW, H, N, 64, seed=21, scale=1.0))
+    plain = fa.window_attn_fwd_cute(q, k, v, group_ids=ids.cuda())            # fallback-capable kernel
+    tagged = fa.window_attn_fwd_cute(q, k, v, group_ids=mark_region_ids_fit(ids.cuda()))
+    assert torch.equal(plain, tagged)
+    lib = _lib.load()
+    _lib.check(lib.fa_attention_status_reset(None), "status reset")
+    bad = torch.randint(0, 40, (nW, N), generator=g).to(torch.uint8)
+    assert not region_ids_fit(bad.numpy())
+    fa.window_attn_fwd_cute(q, k, v, group_ids=mark_region_ids_fit(bad.cuda()))
+    torch.cuda.synchronize()
+    st = ctypes.c_int(-1)
+    _lib.check(lib.fa_attention_status(ctypes.byref(st)), "status")
+    assert st.value == 28
+    _lib.check(lib.fa_attention_status_reset(None), "status reset")
