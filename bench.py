@@ -261,8 +261,10 @@ def run_b200(args) -> None:
     # dram__bytes_read + dram__bytes_write = 0.973-0.979 x the algorithmic bytes (Q, K, V once,
     # part of O still in L2 at exit); the same ratio is applied to this step's average launch.
     traffic = round(TRAFFIC_RATIO * attn_bytes / attn_launches) if attn_launches else None
-    # Per block: partition, attention, unmerge+AdaLN1, GELU, AdaLN2.
-    per_step_launches = 5 * (sum(CONFIG4["encoder_depths"]) + sum(CONFIG4["decoder_depths"]))
+    # Per block: attention, unmerge+AdaLN1, GELU, AdaLN2 (fused with the next block's partition);
+    # plus the partition of the first block of each of the 6 stages.
+    n_blocks = sum(CONFIG4["encoder_depths"]) + sum(CONFIG4["decoder_depths"])
+    per_step_launches = 4 * n_blocks + len(CONFIG4["encoder_depths"]) + len(CONFIG4["decoder_depths"])
     line = {
         "metric": METRIC, "value": round(ms, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": False, "scaling": "weak",

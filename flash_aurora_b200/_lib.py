@@ -37,6 +37,8 @@ SIGNATURES = {
     "fa_roll_pad_partition": (_i32, [_vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
     "fa_crop_roll_unmerge": (_i32, [_vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
     "fa_adaln_film": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _f32, _f32, _vp, _i32, _vp, _i64, _i64, _i64, _vp]),
+    "fa_adaln_film_partition": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _f32, _f32, _vp, _i32, _vp, _i32,
+                                       _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
     "fa_unmerge_adaln_film": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _f32, _f32, _vp, _i32, _vp,
                                      _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
     "fa_roll_pad_partition_band": (_i32, [_vp, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64,

@@ -21,6 +21,7 @@ __all__ = [
     "adaptive_layernorm_film_add_residual_forward",
     "unmerge_adaptive_layernorm_film_add_residual",
     "unmerge_adaptive_layernorm_film_add_residual_band",
+    "adaptive_layernorm_film_add_residual_partition",
 ]
 
 _MAX_D = 2048
@@ -213,4 +214,47 @@ def unmerge_adaptive_layernorm_film_add_residual_band(
         out_bf16.data_ptr() if out_bf16 is not None else None, B, C, Hb, field_res[1], W, D,
         _lib.i32x3(window_size), _lib.i32x3(shift_size), _lib.stream_ptr(residual.device))
     _lib.check(rc, "unmerge_adaptive_layernorm_film_add_residual_band")
+    return out
+
+
+def adaptive_layernorm_film_add_residual_partition(
+    residual: torch.Tensor,
+    x: torch.Tensor,
+    scale: torch.Tensor,
+    shift: torch.Tensor,
+    res: tuple[int, int, int],
+    window_size: tuple[int, int, int],
+    shift_size: tuple[int, int, int],
+    windows: torch.Tensor,
+    scale_bias: float = 0.0,
+    eps: float = 1e-5,
+) -> torch.Tensor:
+    """``out = residual + AdaLN(x)`` (fp32) that also writes ``out`` into ``windows`` in the layout
+    of ``roll_pad_partition_windows(out, res, window_size, shift_size)`` (rounded to the windows'
+    dtype): norm2 of one block fused with the partition of the next. Only token slots are written;
+    ``windows`` must hold zeros in its pad slots (a zero-filled buffer reused across blocks)."""
+    if residual.device.type != "cuda" or x.device.type != "cuda":
+        raise ValueError("adaptive_layernorm_film_add_residual_partition requires CUDA tensors.")
+    if residual.dtype != torch.float32 or x.dtype not in _DTYPES or residual.shape != x.shape:
+        raise ValueError("residual must be float32 and x float32/bfloat16 of the same shape")
+    C, H, W = (int(v) for v in res)
+    B, L, D = x.shape
+    if L != C * H * W:
+        raise ValueError(f"x has {L} tokens, res {tuple(res)} has {C * H * W}")
+    if D > _MAX_D:
+        raise ValueError(f"AdaLN supports D <= {_MAX_D}")
+    _, _, _, _, nW, N = window_geometry(tuple(res), tuple(window_size), tuple(shift_size))
+    if (tuple(windows.shape) != (B * nW, N, D) or windows.dtype not in _DTYPES or not windows.is_contiguous()
+            or windows.device != x.device):
+        raise ValueError(f"windows must be a contiguous float32/bfloat16 tensor of shape {(B * nW, N, D)}")
+    scale = _mod_rows(scale, B, D, "scale")
+    shift = _mod_rows(shift, B, D, "shift").to(scale.dtype)
+    x, residual = x.contiguous(), residual.contiguous()
+    out = torch.empty(B, L, D, device=x.device, dtype=torch.float32)
+    rc = _lib.load().fa_adaln_film_partition(
+        x.data_ptr(), _lib.dtype_code(x.dtype), residual.data_ptr(), _lib.FA_F32, scale.data_ptr(),
+        shift.data_ptr(), _lib.dtype_code(scale.dtype), float(scale_bias), float(eps), out.data_ptr(), _lib.FA_F32,
+        windows.data_ptr(), _lib.dtype_code(windows.dtype), B, C, H, W, D, _lib.i32x3(window_size),
+        _lib.i32x3(shift_size), _lib.stream_ptr(x.device))
+    _lib.check(rc, "adaptive_layernorm_film_add_residual_partition")
     return out

@@ -51,6 +51,11 @@ struct AdaArgs {
   bool gather;
   LayoutParams lp;
   const void* halo_in;  // band mode: halo-back rows of the first lp.band band rows (x dtype)
+  // Optional scatter of the output rows into the window layout of the next block (its
+  // roll + pad + partition); pad slots are left untouched (the caller keeps them zero).
+  void* win_out;
+  bool win_bf16;
+  LayoutParams wlp;
 };
 
 // kChunks = number of 8-element (vector path) or 1-element (scalar path) chunks per lane.
@@ -83,6 +88,14 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) adaln_kernel(AdaArgs a) {
         xg = reinterpret_cast<const TX*>(a.halo_in);
         xrow = b * (int64_t)a.lp.C * a.lp.band * a.lp.W + (-1 - slot);
       }
+    }
+    int64_t wrow = -1;
+    if (a.win_out) {
+      const int32_t t = (int32_t)(row - b * a.L);
+      const int32_t w = t % a.wlp.W;
+      const int32_t h = (t / a.wlp.W) % a.wlp.H;
+      const int32_t c = t / (a.wlp.W * a.wlp.H);
+      wrow = b * (int64_t)a.wlp.nW * a.wlp.N + unmerge_slot(a.wlp, c, h, w);
     }
     const TX* xr = xg + xrow * D;
     float v[kChunks][kE];
@@ -134,6 +147,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) adaln_kernel(AdaArgs a) {
         }
         Vec8<TO>::store(og + row * D + col, y);
         if (a.out_bf16) Vec8<__nv_bfloat16>::store(a.out_bf16 + row * D + col, y);
+        if (wrow >= 0) {
+          if (a.win_bf16) Vec8<__nv_bfloat16>::store(reinterpret_cast<__nv_bfloat16*>(a.win_out) + wrow * D + col, y);
+          else Vec8<float>::store(reinterpret_cast<float*>(a.win_out) + wrow * D + col, y);
+        }
       } else {
         const float sc = load_mod1(a.scale, a.mod_bf16, mrow + col);
         const float sh = load_mod1(a.shift, a.mod_bf16, mrow + col);
@@ -141,6 +158,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) adaln_kernel(AdaArgs a) {
         if (rg) y[0] += to_f32(rg[row * D + col]);
         og[row * D + col] = from_f32<TO>(y[0]);
         if (a.out_bf16) a.out_bf16[row * D + col] = __float2bfloat16_rn(y[0]);
+        if (wrow >= 0) {
+          if (a.win_bf16) reinterpret_cast<__nv_bfloat16*>(a.win_out)[wrow * D + col] = __float2bfloat16_rn(y[0]);
+          else reinterpret_cast<float*>(a.win_out)[wrow * D + col] = y[0];
+        }
       }
     }
   }
@@ -186,7 +207,8 @@ int run_adaln(AdaArgs a, int x_dtype, int residual_dtype, int mod_dtype, int out
   a.mod_bf16 = mod_dtype == FA_BF16;
   const bool vec = (a.D % 8 == 0) && aligned16(a.x) && aligned16(a.scale) && aligned16(a.shift) &&
                    aligned16(a.out) && (!a.residual || aligned16(a.residual)) &&
-                   (!a.out_bf16 || aligned16(a.out_bf16)) && (!a.halo_in || aligned16(a.halo_in));
+                   (!a.out_bf16 || aligned16(a.out_bf16)) && (!a.halo_in || aligned16(a.halo_in)) &&
+                   (!a.win_out || aligned16(a.win_out));
   if (x_dtype == FA_F32) return launch_adaln<float, float>(a, vec, s);
   if (out_dtype == FA_F32) return launch_adaln<__nv_bfloat16, float>(a, vec, s);
   return launch_adaln<__nv_bfloat16, __nv_bfloat16>(a, vec, s);
@@ -250,4 +272,27 @@ extern "C" int fa_unmerge_adaln_film_band(const void* windows, const void* halo_
   FA_REQUIRE(halo_in || a.lp.band == 0 || B == 0 || D == 0, FA_ERR_INVALID,
              "shifted band needs the halo-back rows");
   return run_adaln(a, windows_dtype, residual_dtype, mod_dtype, out_dtype, (cudaStream_t)stream);
+}
+
+extern "C" int fa_adaln_film_partition(const void* x, int x_dtype, const void* residual, int residual_dtype,
+                                       const void* scale, const void* shift, int mod_dtype, float scale_bias,
+                                       float eps, void* out, int out_dtype, void* windows, int windows_dtype,
+                                       int64_t B, int64_t C, int64_t H, int64_t W, int64_t D,
+                                       const int32_t window_size[3], const int32_t shift_size[3],
+                                       void* stream) {
+  Geometry g;
+  int rc = make_geometry(C, H, W, window_size, shift_size, &g);
+  if (rc != FA_OK) return rc;
+  FA_REQUIRE(D < (1 << 30), FA_ERR_INVALID, "D too large");
+  FA_REQUIRE(windows_dtype == FA_F32 || windows_dtype == FA_BF16, FA_ERR_INVALID,
+             "windows dtype must be FA_F32 or FA_BF16");
+  FA_REQUIRE(windows || B * C * H * W == 0 || D == 0, FA_ERR_INVALID, "null windows pointer");
+  AdaArgs a{};
+  a.x = x; a.residual = residual; a.scale = scale; a.shift = shift;
+  a.scale_bias = scale_bias; a.eps = eps; a.out = out;
+  a.B = B; a.L = C * H * W; a.D = (int32_t)D; a.gather = false;
+  a.win_out = windows;
+  a.win_bf16 = windows_dtype == FA_BF16;
+  a.wlp = layout_params(g);
+  return run_adaln(a, x_dtype, residual_dtype, mod_dtype, out_dtype, (cudaStream_t)stream);
 }

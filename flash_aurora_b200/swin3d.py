@@ -38,13 +38,14 @@ import torch.nn.functional as F
 
 from .adaln import (
     adaptive_layernorm_film_add_residual_forward,
+    adaptive_layernorm_film_add_residual_partition,
     unmerge_adaptive_layernorm_film_add_residual,
     unmerge_adaptive_layernorm_film_add_residual_band,
 )
 from .activation import gelu_erf
 from .sharding import BandContext
 from .swin3d_layout import band_halo_extract, roll_pad_partition_windows, roll_pad_partition_windows_band
-from .util import maybe_adjust_windows
+from .util import maybe_adjust_windows, window_geometry
 from .window_attn import shifted_window_group_ids, window_attn_fwd_cute_qkvpacked
 from .workspace_pool import InferenceWorkspacePool
 
@@ -177,13 +178,20 @@ class Swin3DTransformerBlock(nn.Module):
         return self._bf16.get(lin.weight), (self._bf16.get(lin.bias) if lin.bias is not None else None)
 
     def forward(self, x: torch.Tensor, c: torch.Tensor, res, rollout_step: int = 0,
-                warped: bool = True, band: Optional[BandContext] = None) -> torch.Tensor:
+                warped: bool = True, band: Optional[BandContext] = None,
+                windows: Optional[torch.Tensor] = None,
+                next_windows: Optional[tuple] = None) -> torch.Tensor:
         """``x (B, C*H*W, D)`` fp32, ``c (B, ctx)`` -> ``(B, C*H*W, D)`` fp32.
 
         With ``band`` (a :class:`~flash_aurora_b200.sharding.BandContext`), ``x`` and ``res`` are
         this rank's latitude band of the field ``band.field_res``: the window geometry and mask are
         the field's, a shifted block exchanges its half-window halo rows with the neighbouring
         bands, and the result equals the band's rows of the unsharded block.
+
+        ``windows``: this block's partition of ``x``, already written by the previous block's
+        norm2 (the partition is then skipped). ``next_windows = (shift_size, buffer)``: also write
+        the output into ``buffer`` in the window layout of a following block with that shift
+        (same window size); ``buffer`` keeps zeros in its pad slots.
         """
         if not x.is_cuda:
             raise RuntimeError("Swin3DTransformerBlock.forward requires CUDA tensors (no CPU path).")
@@ -211,7 +219,11 @@ class Swin3DTransformerBlock(nn.Module):
         eps = float(self.norm1.ln.eps)
         with _matmul_tf32(self.precision == "tf32"):
             x5 = x.view(B, C, H, W, D)
-            if band is None:
+            if windows is not None:
+                if band is not None:
+                    raise ValueError("prepartitioned windows are not used with latitude bands")
+                xw = windows
+            elif band is None:
                 xw = roll_pad_partition_windows(x5, res, self.window_size, self.shift_size, out_dtype=act)
             else:
                 halo = band.halo_forward(x5, ss[1]) if ss[1] else None
@@ -241,6 +253,12 @@ class Swin3DTransformerBlock(nn.Module):
             h = gelu_erf(h, inplace=True)
             w2, b2 = self._w(self.mlp.fc2, bf16)
             h = F.linear(h, w2, b2)
+            if next_windows is not None:
+                if band is not None:
+                    raise ValueError("next-block windows are not produced with latitude bands")
+                next_shift, buf = next_windows
+                return adaptive_layernorm_film_add_residual_partition(
+                    x1, h, sc2, sh2, res, self.window_size, next_shift, buf, float(self.norm2.scale_bias), eps)
             return adaptive_layernorm_film_add_residual_forward(
                 x1, h, sc2, sh2, float(self.norm2.scale_bias), eps, output_fp32=True)
 
@@ -318,13 +336,37 @@ class BasicLayer3D(nn.Module):
         with a patch merge or split is not sharded: those change the band geometry)."""
         if band is not None and (self.downsample is not None or self.upsample is not None):
             raise ValueError("latitude-band sharding covers block stacks without patch merge/split")
-        for blk in self.blocks:
-            x = blk(x, c, res, rollout_step, band=band)
+        if band is not None or not x.is_cuda:
+            for blk in self.blocks:
+                x = blk(x, c, res, rollout_step, band=band)
+        else:
+            # Each block's norm2 also writes the next block's windows (norm2 + partition fused);
+            # one zero-filled buffer per stage keeps the pad slots zero.
+            windows = None
+            for i, blk in enumerate(self.blocks):
+                nxt = self.blocks[i + 1] if i + 1 < len(self.blocks) else None
+                buf = self._window_buffer(x, res, nxt) if nxt is not None else None
+                x = blk(x, c, res, rollout_step, windows=windows,
+                        next_windows=(nxt.shift_size, buf) if nxt is not None else None)
+                windows = buf
         if self.downsample is not None:
             return self.downsample(x, res), x
         if self.upsample is not None:
             return self.upsample(x, res, crop), x
         return x, None
+
+    def _window_buffer(self, x: torch.Tensor, res, blk: "Swin3DTransformerBlock") -> torch.Tensor:
+        """Zero-filled ``(B * nW, N, D)`` window buffer for ``blk``'s geometry, kept per shape."""
+        B, _, D = x.shape
+        act = torch.bfloat16 if blk.precision == "bf16_mixed" else torch.float32
+        _, _, _, _, nW, N = window_geometry(tuple(res), blk.window_size, blk.shift_size)
+        key = (B, tuple(res), blk.window_size, D, act, str(x.device))
+        cache = self.__dict__.setdefault("_win_bufs", {})
+        buf = cache.get(key)
+        if buf is None:
+            buf = torch.zeros(B * nW, N, D, dtype=act, device=x.device)
+            cache[key] = buf
+        return buf
 
     def init_respostnorm(self) -> None:
         for blk in self.blocks:

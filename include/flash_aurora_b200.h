@@ -105,6 +105,20 @@ int fa_unmerge_adaln_film(const void* windows, int windows_dtype, const void* re
                           const int32_t window_size[3], const int32_t shift_size[3], void* stream);
 
 /*
+ * fa_adaln_film that also scatters every output row, in windows_dtype, into the window layout
+ * (B * nW, N, D) that fa_roll_pad_partition would produce from `out` for (window_size,
+ * shift_size): the norm2 of one block fused with the partition of the next. Only token slots are
+ * written; the caller keeps the pad slots of `windows` zero (for example one zero-filled buffer
+ * reused by every block of a stage). x, residual, out: (B, C*H*W, D). No counterpart in the
+ * reference (there, swin3d.py:800-815 is followed by the next block's partition, :742-750).
+ */
+int fa_adaln_film_partition(const void* x, int x_dtype, const void* residual, int residual_dtype,
+                            const void* scale, const void* shift, int mod_dtype, float scale_bias,
+                            float eps, void* out, int out_dtype, void* windows, int windows_dtype,
+                            int64_t B, int64_t C, int64_t H, int64_t W, int64_t D,
+                            const int32_t window_size[3], const int32_t shift_size[3], void* stream);
+
+/*
  * Latitude-band sharding of a field (C, H_field, W) across ranks: each rank holds a band of
  * H_band whole window rows, x (B, C, H_band, W, D). No reference counterpart: the upstream
  * backbone runs one field per device (its only multi-device path is a pipeline placement,

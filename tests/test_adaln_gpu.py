@@ -82,3 +82,22 @@ def test_unmerge_fused_equals_composition(res, ws, ss, wdt):
     got = fa.unmerge_adaptive_layernorm_film_add_residual(win, resid, scale, shift, res, ws, ss, out_bf16=xb)
     assert torch.equal(got, ref)
     assert torch.equal(xb, ref.bfloat16())
+
+
+@pytest.mark.parametrize("res,shift", [((4, 36, 72), (1, 3, 6)), ((4, 45, 90), (1, 3, 6)), ((4, 45, 90), (0, 0, 0))])
+@pytest.mark.parametrize("wdtype", [torch.bfloat16, torch.float32])
+def test_adaln_partition_fused_equals_adaln_then_partition(res, shift, wdtype):
+    C, H, W = res
+    D, ws = 128, (2, 6, 12)
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(1, C * H * W, D, generator=g).bfloat16().cuda()
+    resid = torch.randn(1, C * H * W, D, generator=g).cuda()
+    scale = (torch.randn(1, 1, D, generator=g) * 0.1).cuda()
+    shf = (torch.randn(1, 1, D, generator=g) * 0.1).cuda()
+    want = fa.adaptive_layernorm_film_add_residual_forward(resid, x, scale, shf, 0.0, output_fp32=True)
+    want_w = fa.roll_pad_partition_windows(want.view(1, C, H, W, D), res, ws, shift, out_dtype=wdtype)
+    from flash_aurora_b200.adaln import adaptive_layernorm_film_add_residual_partition
+    win = torch.zeros_like(want_w)
+    got = adaptive_layernorm_film_add_residual_partition(resid, x, scale, shf, res, ws, shift, win)
+    assert torch.equal(got, want)
+    assert torch.equal(win, want_w)

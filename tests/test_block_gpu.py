@@ -79,3 +79,31 @@ def test_backbone_small_vs_upstream(golden):
     sample = torch.from_numpy(d["sample"])
     assert OB.relative_l2(torch.from_numpy(strided_sample(y32)), sample) <= 1e-5
     assert OB.relative_l2(torch.from_numpy(strided_sample(ybf)), sample) <= 1e-2
+
+
+@pytest.mark.parametrize("precision", ["bf16_mixed", "fp32"])
+@pytest.mark.parametrize("res", [(4, 36, 72), (4, 45, 90)])
+def test_stage_fused_norm2_partition_equals_block_loop(precision, res):
+    """A stage whose blocks hand the next block its windows (norm2 + partition fused) equals the
+    same blocks run one by one, bit for bit (padded and unpadded grids)."""
+    from flash_aurora_b200.swin3d import BasicLayer3D
+
+    torch.manual_seed(3)
+    dim, heads = 128, 2
+    layer = BasicLayer3D(dim=dim, depth=3, num_heads=heads, ws=(2, 6, 12), time_dim=dim, precision=precision)
+    with torch.no_grad():
+        for p in layer.parameters():
+            p.normal_(0.0, 0.02)
+    layer = layer.cuda().eval()
+    C, H, W = res
+    g = torch.Generator().manual_seed(8)
+    x = torch.randn(1, C * H * W, dim, generator=g).cuda()
+    c = torch.randn(1, dim, generator=g).cuda()
+    with torch.no_grad():
+        got, _ = layer(x, c, res)
+        got2, _ = layer(x, c, res)  # buffers reused across calls
+        want = x
+        for blk in layer.blocks:
+            want = blk(want, c, res)
+    assert torch.equal(got, want)
+    assert torch.equal(got2, want)
