@@ -478,6 +478,23 @@ def run_layout_adaln(args) -> None:
                           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                                        "frac": round(gbs / hbm, 3), "peak_kind": kind, "algorithmic_bytes": nbytes}}),
               flush=True)
+    # The block MLP's fc1 + GELU at each stage of config 4: fused tensor-core kernel vs cuBLAS + GELU.
+    _, tf_peak, _ = _peaks()
+    del h
+    for tag, M, K, N in (("S1", 259200, 512, 2048), ("S2", 64800, 1024, 4096), ("S3", 16200, 2048, 8192)):
+        a = torch.randn(M, K, device=dev, generator=g).bfloat16()
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()
+        b = (torch.randn(N, device=dev, generator=g) * 0.02).bfloat16()
+        flops = 2 * M * N * K
+        ms_f = _time_launches(lambda: fa.linear_bias_act(a, w, b, act="gelu"), args.steps, flush=flush)
+        ms_c = _time_launches(lambda: fa.gelu_erf(torch.nn.functional.linear(a, w, b), inplace=True), args.steps,
+                              flush=flush)
+        tf = flops / (ms_f * 1e-3) / 1e12
+        print(json.dumps({"workload": f"config4 {tag} fc1 + GELU fused (M={M}, K={K}, N={N})", "ms": round(ms_f, 4),
+                          "unfused_cublas_plus_gelu_ms": round(ms_c, 4),
+                          "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": tf_peak, "unit": "TFLOP/s",
+                                       "frac": round(tf / tf_peak, 3), "peak_kind": kind}}), flush=True)
+        del a, w, b
 
 
 def main() -> None:

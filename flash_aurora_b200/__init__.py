@@ -16,6 +16,7 @@ PyTorch host layer that mirrors the operator interface of upstream Flash-Aurora:
 """
 
 from .activation import gelu_erf
+from .linear import linear_bias_act
 from .adaln import (
     adaptive_layernorm_film_add_residual_forward,
     adaptive_layernorm_film_forward,
@@ -44,6 +45,7 @@ from .workspace_pool import InferenceWorkspacePool
 
 __all__ = [
     "gelu_erf",
+    "linear_bias_act",
     "adaptive_layernorm_film_add_residual_forward",
     "adaptive_layernorm_film_forward",
     "unmerge_adaptive_layernorm_film_add_residual",

@@ -22,6 +22,7 @@ FA_ATTN_BF16, FA_ATTN_FP32_3XTF32 = 0, 1
 FA_LAYOUT_BHND, FA_LAYOUT_BNC = 0, 1
 FA_GELU_ERFF, FA_GELU_POLY = 0, 1
 FA_ATTN_FLAG_REGIONS_FIT = 1
+FA_ACT_NONE, FA_ACT_GELU = 0, 1
 
 _i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p
 _u32 = ctypes.c_uint
@@ -48,6 +49,9 @@ SIGNATURES = {
                                          _i32p, _i32p, _vp]),
     "fa_unmerge_adaln_film_band": (_i32, [_vp, _vp, _i32, _vp, _i32, _vp, _vp, _i32, _f32, _f32, _vp, _i32, _vp,
                                           _i64, _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
+    "fa_linear_bias_act": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
+    "fa_gemm_status": (_i32, [ctypes.POINTER(ctypes.c_int)]),
+    "fa_gemm_status_reset": (_i32, [_vp]),
     "fa_gelu_erf": (_i32, [_vp, _vp, _i32, _i64, _i32, _vp]),
     "fa_shifted_window_groups": (_i32, [_i64, _i64, _i64, _i32p, _i32p, _i32, _u8p]),
     "fa_window_attention": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64p, _u8p, _u8p, _i64, _f32,

@@ -17,6 +17,7 @@
 //                |GELU| < 1.3e-4 and the result is within 1e-6 of it (PyTorch's 1 + erf form returns
 //                0 there).
 #include "fa_common.cuh"
+#include "gelu.cuh"
 
 namespace fa {
 namespace {
@@ -27,36 +28,6 @@ constexpr int kUnroll = 4;
 __device__ __forceinline__ float gelu_erf(float x) {
   constexpr float kAlpha = 0.70710678118654752440f;  // 1/sqrt(2)
   return x * 0.5f * (1.0f + erff(x * kAlpha));
-}
-
-// Coefficients of q(t) ~ -log2(erfc(t) / 2), lowest order first (fitted, see the file header).
-__constant__ float kGeluQ[10] = {9.999999404e-01f, 1.627912402e+00f, 9.183757305e-01f, 1.486348212e-01f,
-                                 -2.850020491e-02f, 9.230164578e-04f, 1.523754443e-03f, -5.291793495e-04f,
-                                 8.135833923e-05f, -5.036062703e-06f};
-constexpr float kGeluT = 4.0f;
-
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ float2 splat(float v) { return make_float2(v, v); }
-
-// GELU of two elements (FA_GELU_POLY).
-__device__ __forceinline__ float2 gelu2_poly(float2 x) {
-  constexpr float kAlpha = 0.70710678118654752440f;
-  float2 t = __fmul2_rn(make_float2(fabsf(x.x), fabsf(x.y)), splat(kAlpha));
-  const bool in0 = t.x < kGeluT, in1 = t.y < kGeluT;
-  t.x = fminf(t.x, kGeluT);
-  t.y = fminf(t.y, kGeluT);
-  float2 q = splat(kGeluQ[9]);
-#pragma unroll
-  for (int k = 8; k >= 0; --k) q = __ffma2_rn(q, t, splat(kGeluQ[k]));
-  const float2 h = make_float2(in0 ? ex2_approx(-q.x) : 0.f, in1 ? ex2_approx(-q.y) : 0.f);
-  const float2 m = __fmul2_rn(x, h);                                   // x * Phi(x), x < 0
-  const float2 r = __fmul2_rn(x, __ffma2_rn(h, splat(-1.f), splat(1.f)));  // x * (1 - h), x >= 0
-  return make_float2(x.x < 0.f ? m.x : r.x, x.y < 0.f ? m.y : r.y);
 }
 
 template <int kMethod>

@@ -15,7 +15,8 @@ Per block (upstream swin3d.py:706-815, post-norm), precision ``"bf16_mixed"``:
 4. proj linear, bf16 (cuBLAS).
 5. ``fa_unmerge_adaln_film``: crop/un-roll/merge of the proj output fused into
    ``x1 = x + AdaLN1(.)`` (fp32), plus a bf16 copy of ``x1`` for fc1.
-6. fc1 (bf16) -> exact GELU (``fa_gelu_erf``, in place) -> fc2 (bf16).
+6. ``fa_linear_bias_act``: fc1 + bias + exact GELU in one tcgen05 kernel (bf16 out) -> fc2 (bf16,
+   cuBLAS).
 7. ``fa_adaln_film``: ``x2 = x1 + AdaLN2(h)`` (bf16 input, fp32 residual and output).
 
 Every rounding point equals the upstream ``bf16_mixed`` tier (custom_op_paths.py:188-263): the
@@ -43,6 +44,7 @@ from .adaln import (
     unmerge_adaptive_layernorm_film_add_residual_band,
 )
 from .activation import gelu_erf
+from .linear import linear_bias_act
 from .sharding import BandContext
 from .swin3d_layout import band_halo_extract, roll_pad_partition_windows, roll_pad_partition_windows_band
 from .util import maybe_adjust_windows, window_geometry
@@ -249,8 +251,12 @@ class Swin3DTransformerBlock(nn.Module):
                     a, halo_in, x, sc1, sh1, res, field_res, self.window_size, self.shift_size,
                     float(self.norm1.scale_bias), eps, out_bf16=x1_bf16)
             w1, b1 = self._w(self.mlp.fc1, bf16)
-            h = F.linear(x1_bf16 if bf16 else x1, w1, b1)
-            h = gelu_erf(h, inplace=True)
+            if bf16 and b1 is not None and w1.shape[0] % 256 == 0 and w1.shape[1] % 64 == 0:
+                # fc1 + bias + GELU in one tensor-core kernel (GELU on the fp32 sum).
+                h = linear_bias_act(x1_bf16, w1, b1, act="gelu")
+            else:
+                h = F.linear(x1_bf16 if bf16 else x1, w1, b1)
+                h = gelu_erf(h, inplace=True)
             w2, b2 = self._w(self.mlp.fc2, bf16)
             h = F.linear(h, w2, b2)
             if next_windows is not None:

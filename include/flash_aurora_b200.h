@@ -171,6 +171,23 @@ enum { FA_GELU_ERFF = 0, FA_GELU_POLY = 1 };
 int fa_gelu_erf(const void* x, void* out, int dtype, int64_t n, int method, void* stream);
 
 /*
+ * Linear layer with a fused bias and activation on the tensor cores (tcgen05, 128 x 256 tiles):
+ * out[m, n] = act(sum_k a[m, k] * w[n, k] + bias[n]) for a (M, K), w (N, K) (nn.Linear layout),
+ * bias (N), out (M, N), all bf16 and row-major with row strides lda, ldw, ldo (elements), fp32
+ * accumulation, act FA_ACT_NONE or FA_ACT_GELU (exact GELU through the fitted erfc form of
+ * fa_gelu_erf, applied to the fp32 sum). N % 256 == 0, K % 64 == 0, 16-byte aligned rows.
+ * Replaces the fc1 -> nn.GELU() pair of the block MLP (swin3d.py:73-109), where upstream runs a
+ * cuBLAS GEMM (bf16 autocast) and then a separate activation kernel.
+ * fa_gemm_status reads the kernel's status word (0, or the code of the first wait that timed out);
+ * fa_gemm_status_reset clears it (stream-ordered).
+ */
+enum { FA_ACT_NONE = 0, FA_ACT_GELU = 1 };
+int fa_linear_bias_act(const void* a, const void* w, const void* bias, void* out, int64_t M, int64_t N,
+                       int64_t K, int64_t lda, int64_t ldw, int64_t ldo, int act, void* stream);
+int fa_gemm_status(int* status_out);
+int fa_gemm_status_reset(void* stream);
+
+/*
  * Shifted-window region ids of every window token, (nW, N) uint8 written to HOST memory.
  * Tokens i, j of a window attend to each other unmasked iff their ids are equal; otherwise the
  * logit gets the upstream -100 (compute_3d_shifted_window_mask, swin3d.py:526-599, with the

@@ -1,0 +1,73 @@
+"""GPU parity of the tensor-core linear layer with the fused bias + GELU epilogue.
+
+Reference: the same bf16 operands in float64 on the CPU (exact products, exact GELU). The fused
+kernel rounds once (after the GELU); the unfused cuBLAS + GELU path rounds before and after, so the
+fused result must be at least as close to the reference. Bounds: max error <= 1 bf16 ulp of the
+largest output plus the fp32 accumulation error."""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from flash_aurora_b200 import _lib
+from flash_aurora_b200.linear import linear_bias_act
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(x, w, b, act):
+    y = x.double().cpu() @ w.double().cpu().T + b.double().cpu()
+    if act == "gelu":
+        y = 0.5 * y * (1.0 + torch.erf(y / math.sqrt(2.0)))
+    return y
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1000, 512, 512), (4099, 2048, 512), (259, 1536, 1024),
+                                   (16200, 768, 128)])
+@pytest.mark.parametrize("act", ["gelu", "none"])
+def test_linear_bias_act_matches_float64(M, N, K, act):
+    g = torch.Generator().manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g).bfloat16().cuda()
+    w = (torch.randn(N, K, generator=g) * 0.05).bfloat16().cuda()
+    b = (torch.randn(N, generator=g) * 0.1).bfloat16().cuda()
+    got = linear_bias_act(x, w, b, act=act).cpu().double()
+    ref = _ref(x, w, b, act)
+    unfused = F.linear(x, w, b)
+    if act == "gelu":
+        unfused = F.gelu(unfused)
+    unfused = unfused.cpu().double()
+    err = (got - ref).abs()
+    scale = ref.abs().max().item()
+    assert err.max().item() <= scale * 2 ** -8 + 1e-3
+    rel = (err.norm() / ref.norm()).item()
+    rel_unfused = ((unfused - ref).norm() / ref.norm()).item()
+    assert rel <= max(rel_unfused * 1.05, 2e-3)
+
+
+def test_linear_bias_act_batched_input_and_strided_rows():
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(3, 50, 640, generator=g).bfloat16().cuda()[..., :512]  # row stride 640
+    w = (torch.randn(256, 512, generator=g) * 0.05).bfloat16().cuda()
+    b = torch.zeros(256).bfloat16().cuda()
+    got = linear_bias_act(x, w, b)
+    assert got.shape == (3, 50, 256)
+    ref = _ref(x.reshape(-1, 512), w, b, "gelu").reshape(3, 50, 256)
+    assert (got.cpu().double() - ref).abs().max().item() <= ref.abs().max().item() * 2 ** -8 + 1e-3
+
+
+def test_linear_bias_act_rejects_bad_shapes_and_status_clean():
+    import ctypes
+    x = torch.randn(10, 64).bfloat16().cuda()
+    with pytest.raises(ValueError):
+        linear_bias_act(x, torch.randn(100, 64).bfloat16().cuda(), torch.zeros(100).bfloat16().cuda())
+    with pytest.raises(ValueError):
+        linear_bias_act(x.float(), torch.randn(256, 64).cuda(), torch.zeros(256).cuda())
+    linear_bias_act(x, torch.randn(256, 64).bfloat16().cuda(), torch.zeros(256).bfloat16().cuda())
+    torch.cuda.synchronize()
+    st = ctypes.c_int(-1)
+    _lib.check(_lib.load().fa_gemm_status(ctypes.byref(st)), "status")
+    assert st.value == 0
