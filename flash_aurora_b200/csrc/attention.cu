@@ -989,11 +989,11 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
         pk[k >> 1] = pack_bf16x2(a, b);
       }
       const float pl = (l8[0] + l8[1]) + (l8[2] + l8[3]);
+      // The row sum is only needed by the epilogue (1/l): publish this half's sum now and collect
+      // the partner's after P is handed to the tensor cores, off the path to the PV UMMAs.
       xsum[g * 128 + row] = pl;
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kXSum));
-      if (!mbar_wait(BAR(kXSum), (uint32_t)(i & 1), abort, p.status, 25, kTimeoutNs)) { ok = false; break; }
-      const float l = pl + xsum[(g ^ 1) * 128 + row];
       if (!mbar_wait(BAR(kPEmpty), (uint32_t)((i & 1) ^ 1), abort, p.status, 21, kTimeoutNs)) { ok = false; break; }
 #pragma unroll
       for (int jj = 0; jj < 9; ++jj) {
@@ -1005,6 +1005,10 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kPFull));
+      // The partner reads this slot before it arrives at the next tile's max exchange, which this
+      // warpgroup waits for before writing the slot again.
+      if (!mbar_wait(BAR(kXSum), (uint32_t)(i & 1), abort, p.status, 25, kTimeoutNs)) { ok = false; break; }
+      const float l = pl + xsum[(g ^ 1) * 128 + row];
       if (j_prev >= 0 && !epilogue(j_prev, t_prev, l_prev)) { ok = false; break; }
       j_prev = i;
       t_prev = t;
