@@ -448,7 +448,7 @@ constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // {max, sum} x warpgroup x row
 constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColS2 = 160, kColO0 = 320, kColO1 = 384, kColO2 = 448;
-constexpr int kNumBars = 32;
+constexpr int kNumBars = 34;
 constexpr int kSmem = kStages * kStageBytes + kPBytes + kMaskBytes + kXchgBytes + kNumBars * 8 + 16 + 16 + 1024;
 static_assert(kSmem <= 227 * 1024, "shared memory budget");
 constexpr uint32_t kIdescS = ptx::make_idesc(1, 128, kMaxN, false, false);
@@ -463,7 +463,7 @@ constexpr uint32_t kLaneHalf = 16u << 16;
 
 enum { kFullQK = 0, kEmptyQK = 3, kFullV = 6, kEmptyV = 9, kSFull = 12, kSFree = 13, kPFull = 14, kPEmpty = 15,
        kOFull = 16, kOFree = 18, kO2Full = 20, kO2Free = 22, kDone = 24, kXMax = 25, kXSum = 26,
-       kMaskFull = 27, kMaskEmpty = 29 };
+       kMaskFull = 27, kMaskEmpty = 29, kOStaged = 31 };
 
 // Byte offset of bf16 element e (0..15) of row r in a 32-byte-swizzled K-major tile.
 __device__ __forceinline__ uint32_t sw32_offset(int r, int e) {
@@ -637,7 +637,8 @@ __device__ __forceinline__ float raw_logits72(uint32_t (&v)[72], const uint32_t 
 template <int kMask, bool kFullN>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                    const __grid_constant__ CUtensorMap tmv, const Params p) {
+                    const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmo,
+                    const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -684,6 +685,8 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       mbar_init(BAR(kMaskFull + b), 1);
       mbar_init(BAR(kMaskEmpty + b), 1);
     }
+    // A tile's output rows are staged in its V slot once PV is done: 8 softmax warps + warp 3.
+    for (int s = 0; s < kStages; ++s) mbar_init(BAR(kOStaged + s), 9);
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -769,7 +772,24 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       if (lane == 0) {
         const int s = i % kStages;
         const uint32_t ph = (uint32_t)((i / kStages) & 1);
-        if (!mbar_wait(BAR(empty0 + s), ph ^ 1u, abort, p.status, 11, kTimeoutNs)) {
+        bool ready;
+        if (qk) {
+          ready = mbar_wait(BAR(empty0 + s), ph ^ 1u, abort, p.status, 11, kTimeoutNs);
+        } else {
+          // The V slot still holds the staged output of tile i - kStages: store it, and wait
+          // until the copy has read the slot, before loading V of tile i into it.
+          ready = true;
+          if (i >= kStages) {
+            const int jo = i - kStages, to = t_begin + jo;
+            ready = mbar_wait(BAR(kOStaged + s), (uint32_t)((jo / kStages) & 1), abort, p.status, 14, kTimeoutNs);
+            if (ready) {
+              tma_store_4d(&tmo, sbase + s * kStageBytes + (uint32_t)kQKBytes, 0, 0, to % p.H, to / p.H);
+              bulk_commit_group();
+              bulk_wait_group_read0();
+            }
+          }
+        }
+        if (!ready) {
           ok = 0;
         } else {
           const uint32_t dst = sbase + s * kStageBytes + (qk ? 0u : (uint32_t)kQKBytes);
@@ -789,6 +809,16 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       int no_abort = 0;
       for (int s = 0; s < kStages; ++s)
         if (last_par[s] >= 0) mbar_wait(BAR(full0 + s), (uint32_t)last_par[s], &no_abort, p.status, 12, kTimeoutNs);
+      if (!qk) {
+        // Outputs of the last tiles (bounded waits; skipped after an abort).
+        for (int jo = n_local > kStages ? n_local - kStages : 0; jo < n_local; ++jo) {
+          const int s = jo % kStages, to = t_begin + jo;
+          if (!mbar_wait(BAR(kOStaged + s), (uint32_t)((jo / kStages) & 1), abort, p.status, 15, kTimeoutNs)) break;
+          tma_store_4d(&tmo, sbase + s * kStageBytes + (uint32_t)kQKBytes, 0, 0, to % p.H, to / p.H);
+          bulk_commit_group();
+        }
+        bulk_wait_group0();
+      }
     }
   } else if (warp == 1) {
     // ---------------- UMMA issuer (event loop) ----------------
@@ -867,7 +897,6 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
             umma_commit(BAR(kOFull + ob));
             umma_commit(BAR(kO2Full + ob));
             umma_commit(BAR(kPEmpty));
-            umma_commit(BAR(kEmptyV + s));
             ++npv;
             progressed = true;
           }
@@ -914,20 +943,24 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kOFree + ob));
-      if (row < p.N) {
-        const int w = t / p.H, h = t - w * p.H;
-        const float inv = 1.f / l;
-        uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)w * p.os_w +
-                                            (int64_t)h * p.os_h + (int64_t)row * p.os_n + 32 * g);
-        uint32_t pk[16];
+      // Stage the row (columns 32g .. 32g+31) in this tile's V slot, 128-byte swizzle; warp 2
+      // writes the whole tile with one bulk tensor store (rows past N are dropped by it).
+      (void)t;
+      const float inv = 1.f / l;
+      uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pk[e] = pack_bf16x2(__uint_as_float(o0[2 * e]) * inv, __uint_as_float(o0[2 * e + 1]) * inv);
-          pk[8 + e] = pack_bf16x2(__uint_as_float(o1[2 * e]) * inv, __uint_as_float(o1[2 * e + 1]) * inv);
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) d[c] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      for (int e = 0; e < 8; ++e) {
+        pk[e] = pack_bf16x2(__uint_as_float(o0[2 * e]) * inv, __uint_as_float(o0[2 * e + 1]) * inv);
+        pk[8 + e] = pack_bf16x2(__uint_as_float(o1[2 * e]) * inv, __uint_as_float(o1[2 * e + 1]) * inv);
       }
+      const uint32_t stg = sbase + (j % kStages) * kStageBytes + (uint32_t)kQKBytes + (uint32_t)row * 128u;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        st_shared_v4(stg + (uint32_t)((((4 * g + c) ^ (row & 7)) & 7) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
+                     pk[4 * c + 3]);
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kOStaged + j % kStages));
       return true;
     };
 
@@ -1038,21 +1071,20 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kO2Free + ob));
-      const int w = t / p.H, h = t - w * p.H;
-      __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)w * p.os_w + (int64_t)h * p.os_h;
+      // Rows 128..143 of the tile's staged output (see the softmax epilogue).
+      (void)t;
       const float ia = 1.f / la, ib = 1.f / lb;
-      if (ra < p.N) {
-        uint32_t* d = reinterpret_cast<uint32_t*>(base + (int64_t)ra * p.os_n + 2 * t0);
+      const uint32_t stg = sbase + (j % kStages) * kStageBytes + (uint32_t)kQKBytes;
 #pragma unroll
-        for (int jd = 0; jd < 8; ++jd)
-          d[4 * jd] = pack_bf16x2(__uint_as_float(o[4 * jd]) * ia, __uint_as_float(o[4 * jd + 1]) * ia);
+      for (int jd = 0; jd < 8; ++jd) {
+        st_shared_u32(stg + (uint32_t)ra * 128u + (uint32_t)(((jd ^ (ra & 7)) & 7) << 4) + 4u * t0,
+                      pack_bf16x2(__uint_as_float(o[4 * jd]) * ia, __uint_as_float(o[4 * jd + 1]) * ia));
+        st_shared_u32(stg + (uint32_t)rb * 128u + (uint32_t)(((jd ^ (rb & 7)) & 7) << 4) + 4u * t0,
+                      pack_bf16x2(__uint_as_float(o[4 * jd + 2]) * ib, __uint_as_float(o[4 * jd + 3]) * ib));
       }
-      if (rb < p.N) {
-        uint32_t* d = reinterpret_cast<uint32_t*>(base + (int64_t)rb * p.os_n + 2 * t0);
-#pragma unroll
-        for (int jd = 0; jd < 8; ++jd)
-          d[4 * jd] = pack_bf16x2(__uint_as_float(o[4 * jd + 2]) * ib, __uint_as_float(o[4 * jd + 3]) * ib);
-      }
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kOStaged + j % kStages));
       return true;
     };
 
@@ -1256,10 +1288,15 @@ int make_map(CUtensorMap* map, const void* base, bool f32, int64_t Bwin, int64_t
 template <int kMask>
 int launch_tc_bf16(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p,
                    cudaStream_t s) {
+  // Output map: the (Dh, N, H, Bwin) view of `out` with its strides, box of one tile.
+  CUtensorMap mo;
+  const int64_t ostr[3] = {p.os_w, p.os_h, p.os_n};
+  int rc = make_map(&mo, p.out, false, p.Bwin, p.H, p.N, ostr);
+  if (rc != FA_OK) return rc;
   auto kern = p.N == kMaxN ? tc::attn_tc_bf16_kernel<kMask, true> : tc::attn_tc_bf16_kernel<kMask, false>;
   FA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmem));
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
-  kern<<<grid, tc::kThreads, tc::kSmem, s>>>(mq, mk, mv, p);
+  kern<<<grid, tc::kThreads, tc::kSmem, s>>>(mq, mk, mv, mo, p);
   return check_launch("attn_tc_bf16_kernel");
 }
 
