@@ -529,6 +529,9 @@ __device__ __forceinline__ WindowRegions regions_from_ids(const uint32_t (&ids)[
   return r;
 }
 
+__device__ __noinline__ void build_onehot(uint32_t sA, int lane, uint32_t present, uint32_t bias_bits, uint32_t i0,
+                                          uint32_t i1, uint32_t i2, uint32_t i3, uint32_t i4);
+
 // One 32-byte row of a one-hot operand: `value` (bf16 bits) at element `slot`, zeros elsewhere;
 // slot >= 16 writes a zero row.
 __device__ __forceinline__ void store_onehot_row(uint32_t tile, int r, int slot, uint32_t value) {
@@ -547,6 +550,23 @@ __device__ __forceinline__ void store_onehot_row(uint32_t tile, int r, int slot,
   } else {
     st_shared_v4(row, 0u, 0u, 0u, 0u);
     st_shared_v4(row + 16u, 0u, 0u, 0u, 0u);
+  }
+}
+
+// The one-hot A and B operands of one window, out of line so that the producer's loop stays small.
+__device__ __noinline__ void build_onehot(uint32_t sA, int lane, uint32_t present, uint32_t bias_bits, uint32_t i0,
+                                          uint32_t i1, uint32_t i2, uint32_t i3, uint32_t i4) {
+  const uint32_t sB = sA + kRow32;
+  const uint32_t ids[5] = {i0, i1, i2, i3, i4};
+#pragma unroll 1
+  for (int m = 0; m < 5; ++m) {
+    const int r = lane + 32 * m;
+    if (r < kMaxN) {
+      const uint32_t id = m == 0 ? ids[0] : m == 1 ? ids[1] : m == 2 ? ids[2] : m == 3 ? ids[3] : ids[4];
+      const int slot = id < 32u ? __popc(present & ((1u << id) - 1u)) : 16;
+      store_onehot_row(sA, r, slot, bias_bits);
+      store_onehot_row(sB, r, slot, 0x3F80u);
+    }
   }
 }
 
@@ -751,16 +771,8 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
           if (lane == 0) okw = mbar_wait(BAR(kMaskEmpty + mb), (u & 1u) ^ 1u, abort, p.status, 13, kTimeoutNs);
           if (!__shfl_sync(0xffffffffu, okw, 0)) break;
           if (wr.mode == kModeUmma) {
-            const uint32_t sA = sMask + (uint32_t)mb * kMaskOpBytes, sB = sA + kRow32;
-#pragma unroll
-            for (int m = 0; m < 5; ++m) {
-              const int r = lane + 32 * m;
-              if (r < kMaxN) {
-                const int slot = ids[m] < 32u ? __popc(wr.present & ((1u << ids[m]) - 1u)) : 16;
-                store_onehot_row(sA, r, slot, bias_bits);
-                store_onehot_row(sB, r, slot, 0x3F80u);  // bf16 1.0
-              }
-            }
+            build_onehot(sMask + (uint32_t)mb * kMaskOpBytes, lane, wr.present, bias_bits, ids[0], ids[1], ids[2],
+                         ids[3], ids[4]);
             fence_proxy_async_shared();
           }
           if (lane == 0) mask_mode[mb] = wr.mode;
@@ -967,13 +979,13 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
     bool ok = true;
     for (int i = 0; i < n_local; ++i) {
       const int t = t_begin + i;
-      if constexpr (kMask != kNoMask) {
+      if constexpr (kBitsPath<kMask>) {  // per-logit masks only
         const int w = t / p.H;
         if (w != cached_w) {
           cached_w = w;
           ++wseq;
           int mode = kModeBits;
-          if constexpr (kRegions<kMask>) {
+          if constexpr (kMask == kGroups) {
             // The producer classified the window before its first load (mask buffer wseq & 1).
             if (!mbar_wait(BAR(kMaskFull + (wseq & 1)), (uint32_t)((wseq >> 1) & 1), abort, p.status, 26,
                            kTimeoutNs)) { ok = false; break; }
@@ -1091,18 +1103,14 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
     bool ok = true;
     for (int i = 0; i < n_local; ++i) {
       const int t = t_begin + i;
-      if constexpr (kMask != kNoMask) {
+      if constexpr (kBitsPath<kMask>) {  // per-logit masks only
         const int w = t / p.H;
         if (w != cached_w) {
           cached_w = w;
           ++wseq;
           const int mw = w % p.nW;
           if constexpr (kMask == kGroupsFit) {
-            // The mask is in S (mask UMMA); only wait for the producer's classification so
-            // that this warp follows the same window sequence.
-            if (!mbar_wait(BAR(kMaskFull + (wseq & 1)), (uint32_t)((wseq >> 1) & 1), abort, p.status, 27,
-                           kTimeoutNs)) { ok = false; break; }
-            wmask = false;
+            wmask = false;  // the mask is in S (mask UMMA): nothing to do per window
           } else if constexpr (kMask == kGroups) {
             const uint8_t* gi = p.mask + (int64_t)mw * p.N;
             // Region masks of up to 16 regions are already in S (mask UMMA); the producer
