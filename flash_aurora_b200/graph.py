@@ -1,0 +1,53 @@
+"""A static-shape step (the backbone forward) captured once into a CUDA graph and replayed.
+
+A forecast service runs the backbone on inputs of one shape over and over. Its ~560 kernel
+launches per step cost the host about 13 ms of launch work, which mostly hides behind the GPU's
+~100 ms, but every short gap between kernels is GPU idle time. Replaying a captured graph removes
+those gaps (about 2 % of the step here) and the per-step Python work.
+
+The capture runs ``fn`` a few times on a side stream first, so that every cache the step fills
+lazily (tensor-core weight copies, region ids, window buffers) exists before capture, then records
+one call. The graph reads ``static_input`` and writes ``static_output``; both live as long as the
+object.
+"""
+
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+
+__all__ = ["CapturedStep"]
+
+
+class CapturedStep:
+    """``fn(x) -> y`` captured for inputs shaped like ``example`` (a CUDA tensor)."""
+
+    def __init__(self, fn: Callable[[torch.Tensor], torch.Tensor], example: torch.Tensor, warmup: int = 2) -> None:
+        if not example.is_cuda:
+            raise ValueError("CapturedStep needs a CUDA example input")
+        self.static_input = example.detach().clone()
+        side = torch.cuda.Stream(example.device)
+        side.wait_stream(torch.cuda.current_stream(example.device))
+        with torch.cuda.stream(side):
+            for _ in range(max(1, warmup)):
+                fn(self.static_input)
+        torch.cuda.current_stream(example.device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.static_output = fn(self.static_input)
+
+    def replay(self) -> torch.Tensor:
+        """Run the step on the current contents of ``static_input``; returns ``static_output``
+        (overwritten by the next replay)."""
+        self.graph.replay()
+        return self.static_output
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        """Copy ``x`` into the static input, replay, and return a fresh copy of the output."""
+        if x.shape != self.static_input.shape or x.dtype != self.static_input.dtype:
+            raise ValueError(f"captured for {tuple(self.static_input.shape)} {self.static_input.dtype}, "
+                             f"got {tuple(x.shape)} {x.dtype}")
+        self.static_input.copy_(x)
+        self.graph.replay()
+        return self.static_output.clone()

@@ -35,3 +35,29 @@ def test_pipeline_reuses_output_buffers_in_order():
     HostPipeline(lambda t: t + 0.5, dev).run(xs, [out[i % 2] for i in range(6)])
     torch.cuda.synchronize()
     assert torch.equal(out[0], torch.full((4096,), 4.5)) and torch.equal(out[1], torch.full((4096,), 5.5))
+
+
+def test_captured_backbone_step_matches_eager():
+    """A backbone forward captured as a CUDA graph replays to the eager result, bit for bit, and the
+    call form copies inputs in and outputs out."""
+    from datetime import timedelta
+
+    from flash_aurora_b200.graph import CapturedStep
+    from flash_aurora_b200.swin3d import Swin3DTransformerBackbone, init_random_weights_
+
+    dev = torch.device("cuda", 0)
+    model = Swin3DTransformerBackbone(embed_dim=128, encoder_depths=(2, 2), encoder_num_heads=(2, 4),
+                                      decoder_depths=(2, 2), decoder_num_heads=(4, 2), window_size=(2, 6, 12),
+                                      precision="bf16_mixed").to(dev).eval()
+    init_random_weights_(model, generator=torch.Generator(device=dev).manual_seed(3))
+    res = (4, 24, 48)
+    g = torch.Generator(device=dev).manual_seed(4)
+    x = torch.randn(1, res[0] * res[1] * res[2], 128, device=dev, generator=g)
+    step = lambda inp: model(inp, lead_time=timedelta(hours=6), rollout_step=0, patch_res=res)
+    with torch.no_grad():
+        want = step(x)
+        graphed = CapturedStep(step, x)
+        assert torch.equal(graphed.replay(), want)
+        x2 = torch.randn(x.shape, device=dev, generator=g)
+        assert torch.equal(graphed(x2), step(x2))
+        assert torch.equal(graphed(x), want)
