@@ -52,6 +52,8 @@ SIGNATURES = {
     "fa_linear_bias_act": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
     "fa_gemm_status": (_i32, [ctypes.POINTER(ctypes.c_int)]),
     "fa_gemm_status_reset": (_i32, [_vp]),
+    "fa_patch_merge_ln": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp]),
+    "fa_patch_split_ln": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32p, _f32, _vp]),
     "fa_gelu_erf": (_i32, [_vp, _vp, _i32, _i64, _i32, _vp]),
     "fa_shifted_window_groups": (_i32, [_i64, _i64, _i64, _i32p, _i32p, _i32, _u8p]),
     "fa_window_attention": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64p, _u8p, _u8p, _i64, _f32,

@@ -43,6 +43,7 @@ from .adaln import (
     unmerge_adaptive_layernorm_film_add_residual,
     unmerge_adaptive_layernorm_film_add_residual_band,
 )
+from . import _lib
 from .activation import gelu_erf
 from .linear import linear_bias_act
 from .sharding import BandContext
@@ -182,13 +183,17 @@ class Swin3DTransformerBlock(nn.Module):
     def forward(self, x: torch.Tensor, c: torch.Tensor, res, rollout_step: int = 0,
                 warped: bool = True, band: Optional[BandContext] = None,
                 windows: Optional[torch.Tensor] = None,
-                next_windows: Optional[tuple] = None) -> torch.Tensor:
+                next_windows: Optional[tuple] = None,
+                mods: Optional[tuple] = None) -> torch.Tensor:
         """``x (B, C*H*W, D)`` fp32, ``c (B, ctx)`` -> ``(B, C*H*W, D)`` fp32.
 
         With ``band`` (a :class:`~flash_aurora_b200.sharding.BandContext`), ``x`` and ``res`` are
         this rank's latitude band of the field ``band.field_res``: the window geometry and mask are
         the field's, a shifted block exchanges its half-window halo rows with the neighbouring
         bands, and the result equals the band's rows of the unsharded block.
+
+        ``mods``: ``(shift1, scale1, shift2, scale2)`` of the two norms, computed for all blocks at
+        once by the backbone (otherwise each norm computes its own).
 
         ``windows``: this block's partition of ``x``, already written by the previous block's
         norm2 (the partition is then skipped). ``next_windows = (shift_size, buffer)``: also write
@@ -216,8 +221,11 @@ class Swin3DTransformerBlock(nn.Module):
         bf16 = self.precision == "bf16_mixed"
         act = torch.bfloat16 if bf16 else torch.float32
         heads = self.num_heads
-        sh1, sc1 = self.norm1.modulation(c)
-        sh2, sc2 = self.norm2.modulation(c)
+        if mods is not None:
+            sh1, sc1, sh2, sc2 = mods
+        else:
+            sh1, sc1 = self.norm1.modulation(c)
+            sh2, sc2 = self.norm2.modulation(c)
         eps = float(self.norm1.ln.eps)
         with _matmul_tf32(self.precision == "tf32"):
             x5 = x.view(B, C, H, W, D)
@@ -282,6 +290,16 @@ class PatchMerging3D(nn.Module):
         C, H, W = input_resolution
         B, L, D = x.shape
         assert L == C * H * W and H > 1 and W > 1
+        if x.dtype == torch.float32 and D % 8 == 0 and 4 * D <= 4096:
+            # pad + 2x2 gather + LayerNorm(4D) in one kernel (fa_patch_merge_ln)
+            x = x.contiguous()
+            out = torch.empty(B, C * ((H + 1) // 2) * ((W + 1) // 2), 4 * D, device=x.device, dtype=torch.float32)
+            rc = _lib.load().fa_patch_merge_ln(
+                x.data_ptr(), out.data_ptr(), self.norm.weight.float().contiguous().data_ptr(),
+                self.norm.bias.float().contiguous().data_ptr(), B, C, H, W, D, float(self.norm.eps),
+                _lib.stream_ptr(x.device))
+            _lib.check(rc, "PatchMerging3D")
+            return self.reduction(out)
         x = x.view(B, C, H, W, D)
         x = F.pad(x, (0, 0, 0, W % 2, 0, H % 2))  # swin3d.py:839: a 1-token pad goes to the back
         nH, nW = x.shape[2], x.shape[3]
@@ -306,6 +324,18 @@ class PatchSplitting3D(nn.Module):
         x = self.lin1(x)
         B, L, D = x.shape
         assert L == C * H * W and D % 4 == 0
+        Dq = D // 4
+        if x.dtype == torch.float32 and Dq % 8 == 0 and Dq <= 4096:
+            # 2x2 split + crop + LayerNorm(D/4) in one kernel (fa_patch_split_ln)
+            cC, cH, cW = (int(v) for v in crop)
+            x = x.contiguous()
+            out = torch.empty(B, (C - cC) * (2 * H - cH) * (2 * W - cW), Dq, device=x.device, dtype=torch.float32)
+            rc = _lib.load().fa_patch_split_ln(
+                x.data_ptr(), out.data_ptr(), self.norm.weight.float().contiguous().data_ptr(),
+                self.norm.bias.float().contiguous().data_ptr(), B, C, H, W, Dq, _lib.i32x3((cC, cH, cW)),
+                float(self.norm.eps), _lib.stream_ptr(x.device))
+            _lib.check(rc, "PatchSplitting3D")
+            return self.lin2(out)
         x = x.view(B, C, H, W, 2, 2, D // 4).permute(0, 1, 2, 4, 3, 5, 6).reshape(B, C, 2 * H, 2 * W, D // 4)
         cC, cH, cW = crop
         x = x[:, : x.shape[1] - cC, : x.shape[2] - cH, : x.shape[3] - cW, :]
@@ -337,14 +367,16 @@ class BasicLayer3D(nn.Module):
         self.upsample = upsample(dim=dim) if upsample is not None else None
 
     def forward(self, x, c, res, crop=(0, 0, 0), rollout_step: int = 0,
-                band: Optional[BandContext] = None):
+                band: Optional[BandContext] = None, mods: Optional[list] = None):
         """``band``: run the blocks on this rank's latitude band of the stage's field (a stage
         with a patch merge or split is not sharded: those change the band geometry)."""
         if band is not None and (self.downsample is not None or self.upsample is not None):
             raise ValueError("latitude-band sharding covers block stacks without patch merge/split")
+        if mods is None:
+            mods = [None] * len(self.blocks)
         if band is not None or not x.is_cuda:
-            for blk in self.blocks:
-                x = blk(x, c, res, rollout_step, band=band)
+            for blk, m in zip(self.blocks, mods):
+                x = blk(x, c, res, rollout_step, band=band, mods=m)
         else:
             # Each block's norm2 also writes the next block's windows (norm2 + partition fused);
             # one zero-filled buffer per stage keeps the pad slots zero.
@@ -353,7 +385,7 @@ class BasicLayer3D(nn.Module):
                 nxt = self.blocks[i + 1] if i + 1 < len(self.blocks) else None
                 buf = self._window_buffer(x, res, nxt) if nxt is not None else None
                 x = blk(x, c, res, rollout_step, windows=windows,
-                        next_windows=(nxt.shift_size, buf) if nxt is not None else None)
+                        next_windows=(nxt.shift_size, buf) if nxt is not None else None, mods=mods[i])
                 windows = buf
         if self.downsample is not None:
             return self.downsample(x, res), x
@@ -450,6 +482,40 @@ class Swin3DTransformerBackbone(nn.Module):
         padded.append((0, 0, 0))
         return all_res, padded
 
+    def _modulations(self, c: torch.Tensor) -> dict:
+        """(shift1, scale1, shift2, scale2) of every block, from one SiLU and one fp32 GEMM over the
+        concatenated modulation weights of all norms (film.py:82,117: shift first), instead of
+        two tiny GEMVs per block. The concatenation is cached and rebuilt when a weight changes."""
+        norms = []
+        layers = list(self.encoder_layers) + list(self.decoder_layers)
+        for layer in layers:
+            for blk in layer.blocks:
+                norms.extend((blk.norm1, blk.norm2))
+        lins = [n.ln_modulation[1] for n in norms]
+        key = tuple((id(l.weight), l.weight._version, id(l.bias), l.bias._version, str(l.weight.device))
+                    for l in lins)
+        cache = self.__dict__.get("_mod_cat")
+        if cache is None or cache[0] != key:
+            w = torch.cat([l.weight.detach() for l in lins], dim=0).float().contiguous()
+            b = torch.cat([l.bias.detach() for l in lins], dim=0).float().contiguous()
+            cache = (key, w, b, [l.weight.shape[0] for l in lins])
+            self.__dict__["_mod_cat"] = cache
+        _, w, b, sizes = cache
+        with _matmul_tf32(False):
+            allmod = F.linear(F.silu(c.float()), w, b)
+        parts = allmod.unsqueeze(1).split(sizes, dim=-1)
+        out: dict = {}
+        k = 0
+        for layer in layers:
+            per_block = []
+            for _ in layer.blocks:
+                s1, c1 = parts[k].chunk(2, dim=-1)
+                s2, c2 = parts[k + 1].chunk(2, dim=-1)
+                per_block.append((s1.contiguous(), c1.contiguous(), s2.contiguous(), c2.contiguous()))
+                k += 2
+            out[layer] = per_block
+        return out
+
     def time_embedding(self, lead_time: timedelta, batch: int, device) -> torch.Tensor:
         hours = lead_time / timedelta(hours=1)
         lt = torch.full((batch,), hours, dtype=torch.float32, device=device)
@@ -463,16 +529,18 @@ class Swin3DTransformerBackbone(nn.Module):
             raise RuntimeError("Swin3DTransformerBackbone.forward requires CUDA tensors (no CPU path).")
         all_res, padded = self.get_encoder_specs(patch_res)
         c = self.time_embedding(lead_time, x.shape[0], x.device)
+        mods = self._modulations(c)
         # Stage-boundary linears follow the tier: TF32 in bf16_mixed/tf32 (upstream hybrid
         # routing, custom_op_paths.py:234-243), strict FP32 in fp32.
         with _matmul_tf32(self.precision != "fp32"):
             skips = []
             for i, layer in enumerate(self.encoder_layers):
-                x, x_unscaled = layer(x, c, all_res[i], rollout_step=rollout_step)
+                x, x_unscaled = layer(x, c, all_res[i], rollout_step=rollout_step, mods=mods[layer])
                 skips.append(x_unscaled)
             for i, layer in enumerate(self.decoder_layers):
                 index = self.num_decoder_layers - i - 1
-                x, _ = layer(x, c, all_res[index], padded[index - 1], rollout_step=rollout_step)
+                x, _ = layer(x, c, all_res[index], padded[index - 1], rollout_step=rollout_step,
+                             mods=mods[layer])
                 if 0 < i < self.num_decoder_layers - 1:
                     x = x + skips[index - 1]
                 elif i == self.num_decoder_layers - 1:

@@ -188,6 +188,23 @@ int fa_gemm_status(int* status_out);
 int fa_gemm_status_reset(void* stream);
 
 /*
+ * Stage-boundary gathers fused with their LayerNorm (affine weight/bias, fp32):
+ *  - fa_patch_merge_ln: x (B, C, H, W, D) -> out (B, C*ceil(H/2)*ceil(W/2), 4D), the 2 x 2 patch
+ *    of each output token (zero pad at the back of odd H / W; channel (dh*2 + dw)*D + d), then
+ *    LayerNorm(4D). Replaces the pad/permute/LayerNorm of PatchMerging3D (swin3d.py:818-861)
+ *    before its reduction linear.
+ *  - fa_patch_split_ln: z (B, C, H, W, 4*Dq) (the output of PatchSplitting3D's first linear) ->
+ *    out (B, (C-crop0)*(2H-crop1)*(2W-crop2), Dq): sub-token (dh, dw) of each token, crop at the
+ *    back, then LayerNorm(Dq). Replaces the permute/crop/LayerNorm of PatchSplitting3D
+ *    (swin3d.py:864-919) before its second linear.
+ * D, Dq multiples of 8; 4D and Dq at most 4096; 16-byte aligned tensors.
+ */
+int fa_patch_merge_ln(const float* x, float* out, const float* weight, const float* bias, int64_t B, int64_t C,
+                      int64_t H, int64_t W, int64_t D, float eps, void* stream);
+int fa_patch_split_ln(const float* z, float* out, const float* weight, const float* bias, int64_t B, int64_t C,
+                      int64_t H, int64_t W, int64_t Dq, const int32_t crop[3], float eps, void* stream);
+
+/*
  * Shifted-window region ids of every window token, (nW, N) uint8 written to HOST memory.
  * Tokens i, j of a window attend to each other unmasked iff their ids are equal; otherwise the
  * logit gets the upstream -100 (compute_3d_shifted_window_mask, swin3d.py:526-599, with the
