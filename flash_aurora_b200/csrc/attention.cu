@@ -1259,6 +1259,539 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
 }  // namespace tc
 
 // ------------------------------------------------------------------------------------------
+// FP32 I/O kernel on the 5th-generation tensor cores: 3xTF32 with tcgen05.mma kind::tf32.
+//
+// Every operand x is split as x = hi + lo: hi is x with its 13 low mantissa bits cleared (a tf32
+// value, so the tensor core takes it exactly), lo = x - hi (exact in fp32; the tensor core rounds
+// it to tf32). A product a.b accumulates a_lo.b_hi + a_hi.b_lo + a_hi.b_hi in fp32; the dropped
+// a_lo.b_lo term and the rounding of lo leave it within about 2^-21 of the fp32 product, the
+// accuracy of the warp-level 3xTF32 kernel above, unlike the upstream 1xTF32 QK^T + BF16 PV
+// kernel (ops/cute/_kernel_fp32.py:491-493).
+//
+// One (window, head) tile at a time per CTA, single-buffered: shared memory holds hi and lo of
+// Q and K (144 x 32-float blocks with 128-byte swizzle, as TMA writes them) and of V^T. kind::tf32
+// takes K-major operands only (an MN-major tf32 operand yields zeros on B200), so V, which TMA
+// lands in the Q slot once the S products are done, is transposed by the split warps into
+// 64 x 144 K-major blocks: keys 0..127 with 128-byte swizzle, keys 128..143 with 32-byte swizzle.
+//   S  = Q K^T  rows 0..127 (M=128) and rows 80..143 (M=64), N=144, 8 K-steps x 3 products, both
+//               operands K-major in shared memory;
+//   P           the softmax warps write P_hi over S in TMEM (tcgen05.st), then P_lo over P_hi once
+//               the two P_hi products have run;
+//   O  = P V    M=128, N=64, 18 K-steps x 3 products, A (P) from TMEM, V^T in shared memory.
+// A TMEM A operand must sit in the same lanes as its accumulator, so the M=64 block (rows 128..143
+// are its rows 48..63) keeps S, P and O in the first lane half (lanes 0-15 of each 32-lane group).
+// The issuer interleaves the two blocks, so that each block's P_lo store overlaps the other block's
+// products. TMEM columns: S / P 0..143, O 160..223, M=64 block S / P 224..367 and O 384..447.
+// Warp roles (512 threads, one CTA per SM, a contiguous range of tiles per CTA):
+//   warp 0       TMA: Q and K of a tile once V of the previous one is transposed, V once its S
+//                products are done;
+//   warp 1       TMEM owner and UMMA issuer (one thread, blocking on each input);
+//   warp 3       rows 128..143 (16x256b TMEM shape, two rows per thread, quad reductions);
+//   warps 4..11  rows 0..127: two warpgroups of 72 keys per row (row max / sum exchanged through
+//                shared memory), then the output rows (32 columns per warpgroup);
+//   warps 12..15 split Q and K into hi (in place) and lo; transpose and split V.
+// Every wait is bounded (status word + abort flag); warp 2 only takes part in the set-up.
+// ------------------------------------------------------------------------------------------
+namespace tc32 {
+
+constexpr int kBlk = kTileBytes;  // 144 rows x 32 floats (128 bytes)
+constexpr int kMat = 2 * kBlk;    // one 144 x 64 fp32 operand
+// Raw / hi blocks of Q and K are adjacent, and so are their lo blocks: one split pass covers both.
+// V lands in the Q slot (kOffQh); its transposed hi and lo go to kOffVh / kOffVl.
+constexpr int kOffQh = 0, kOffKh = kMat, kOffQl = 2 * kMat, kOffKl = 3 * kMat, kOffVh = 4 * kMat, kOffVl = 5 * kMat;
+// V^T (64 rows of head dims): keys 32b..32b+31 in 128-byte-swizzled blocks b = 0..3 (8 KB each),
+// keys 128..135 and 136..143 in 32-byte-swizzled blocks (2 KB each); kMat bytes in all.
+constexpr int kVtSw32 = 4 * 64 * 128;
+constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // {max, sum} x warpgroup x row
+constexpr int kThreads = 512;
+constexpr int kConvThreads = 128;             // warps 12..15
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColO = 160, kColSR = 224, kColOR = 384;
+constexpr uint32_t kRowOff80 = 80 * 128;
+constexpr uint32_t kHiMask = 0xFFFFE000u;     // sign, exponent and the 10 mantissa bits of tf32
+enum { kQKFull = 0, kQKConv, kVFull, kVConv, kSFull, kPFull, kHiDone, kPLoFull, kPRemHi, kRemHiDone, kPRemLo,
+       kOFull, kOFree, kORemFull, kORemFree, kPVDone, kXMax, kXSum, kDone, kNumBars };
+constexpr int kSmem = 6 * kMat + kXchgBytes + kNumBars * 8 + 16 + 1024;
+static_assert(kSmem <= 227 * 1024, "shared memory budget");
+constexpr uint32_t kIdS = ptx::make_idesc(2, 128, kMaxN, false, false);
+constexpr uint32_t kIdSR = ptx::make_idesc(2, 64, kMaxN, false, false);
+constexpr uint32_t kIdO = ptx::make_idesc(2, 128, 64, false, false);
+constexpr uint32_t kIdOR = ptx::make_idesc(2, 64, 64, false, false);
+
+__device__ __forceinline__ uint32_t hi_of(uint32_t x) { return x & kHiMask; }
+__device__ __forceinline__ uint32_t lo_of(uint32_t x) {
+  return __float_as_uint(__uint_as_float(x) - __uint_as_float(x & kHiMask));
+}
+
+// Byte offset of the 4 keys key..key+3 (key % 4 == 0) of head dim d in the V^T layout.
+__device__ __forceinline__ uint32_t vt_off(int d, int key) {
+  if (key < 128)
+    return (uint32_t)((key >> 5) * 8192 + d * 128 + ((((key & 31) >> 2) ^ (d & 7)) << 4));
+  const int k2 = key - 128;
+  return (uint32_t)(kVtSw32 + (k2 >> 3) * 2048 + d * 32 + ((((k2 & 7) >> 2) ^ ((d >> 2) & 1)) << 4));
+}
+
+// B operand descriptor of PV K-step j (keys 8j..8j+7) in a V^T buffer.
+__device__ __forceinline__ uint64_t vt_desc(uint32_t vt, int j) {
+  return j < 16 ? desc_sw128(vt + (uint32_t)((j >> 2) * 8192 + (j & 3) * 32), 16, 1024)
+                : desc_sw32(vt + (uint32_t)(kVtSw32 + (j - 16) * 2048), 256);
+}
+
+// V (144 keys x 64 dims as TMA wrote it at `raw`) -> hi and lo of V^T. Each thread moves 4 x 4
+// blocks (4 keys x 4 dims); blocks are enumerated along diagonals so that the eight threads of a
+// quarter warp touch eight different 16-byte columns on both sides.
+__device__ __forceinline__ void split_transpose_v(uint32_t raw, uint32_t vh, uint32_t vl, int ct) {
+#pragma unroll 1
+  for (int n = ct; n < 36 * 16; n += kConvThreads) {
+    const int dc = n & 15, kg = ((n >> 4) + dc) % 36;
+    uint32_t x[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int key = 4 * kg + r;
+      ld_shared_v4(raw + (uint32_t)((dc >> 3) * kBlk + key * 128 + (((dc & 7) ^ (key & 7)) << 4)), x[r][0], x[r][1],
+                   x[r][2], x[r][3]);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t o = vt_off(4 * dc + c, 4 * kg);
+      st_shared_v4(vh + o, hi_of(x[0][c]), hi_of(x[1][c]), hi_of(x[2][c]), hi_of(x[3][c]));
+      st_shared_v4(vl + o, lo_of(x[0][c]), lo_of(x[1][c]), lo_of(x[2][c]), lo_of(x[3][c]));
+    }
+  }
+}
+
+// hi (in place) and lo of `bytes` of landed operand blocks; 16 bytes per thread and step.
+__device__ __forceinline__ void split_blocks(uint32_t hi, uint32_t lo, int bytes, int ct) {
+#pragma unroll 4
+  for (int o = ct * 16; o < bytes; o += kConvThreads * 16) {
+    uint32_t a, b, c, d;
+    ld_shared_v4(hi + (uint32_t)o, a, b, c, d);
+    st_shared_v4(hi + (uint32_t)o, hi_of(a), hi_of(b), hi_of(c), hi_of(d));
+    st_shared_v4(lo + (uint32_t)o, lo_of(a), lo_of(b), lo_of(c), lo_of(d));
+  }
+}
+
+template <int kMask, bool kFullN>
+__global__ void __launch_bounds__(kThreads, 1)
+attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                    const __grid_constant__ CUtensorMap tmv, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  float* xchg = reinterpret_cast<float*>(smem + 6 * kMat);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kMat + kXchgBytes);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  const uint32_t bar0 = smem_u32(bars);
+  auto BAR = [&](int slot) -> uint32_t { return bar0 + 8u * (uint32_t)slot; };
+  __shared__ int abort_flag;
+
+  const int t_begin = (int)(((int64_t)blockIdx.x * p.num_tiles) / gridDim.x);
+  const int t_end = (int)(((int64_t)(blockIdx.x + 1) * p.num_tiles) / gridDim.x);
+  const int n_local = t_end - t_begin;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int b = 0; b < kNumBars; ++b) {
+      const uint32_t count = (b == kQKConv || b == kVConv) ? 4u
+                             : (b == kPFull || b == kPLoFull || b == kOFree || b == kXMax || b == kXSum) ? 8u
+                                                                                                           : 1u;
+      mbar_init(BAR(b), count);
+    }
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  volatile int* abort = &abort_flag;
+  const float braw = kMaskedLog2 / p.scale_log2;  // -100 / scale: the mask bias before scaling
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmq);
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      int qk_issued = 0, v_issued = 0;
+      for (int i = 0; i < n_local; ++i) {
+        const int t = t_begin + i, w = t / p.H, h = t - w * p.H;
+        const uint32_t prev = (uint32_t)((i & 1) ^ 1);  // completion of tile i-1 (free on tile 0)
+        // The Q slot holds V of tile i-1 until it is transposed (which follows its S products).
+        if (!mbar_wait(BAR(kVConv), prev, abort, p.status, 41, kTimeoutNs)) break;
+        mbar_arrive_expect_tx(BAR(kQKFull), 2 * kMat);
+        tma_load_4d(sbase + kOffQh, &tmq, BAR(kQKFull), 0, 0, h, w);
+        tma_load_4d(sbase + kOffQh + kBlk, &tmq, BAR(kQKFull), 32, 0, h, w);
+        tma_load_4d(sbase + kOffKh, &tmk, BAR(kQKFull), 0, 0, h, w);
+        tma_load_4d(sbase + kOffKh + kBlk, &tmk, BAR(kQKFull), 32, 0, h, w);
+        ++qk_issued;
+        if (!mbar_wait(BAR(kSFull), (uint32_t)(i & 1), abort, p.status, 42, kTimeoutNs)) break;
+        mbar_arrive_expect_tx(BAR(kVFull), kMat);
+        tma_load_4d(sbase + kOffQh, &tmv, BAR(kVFull), 0, 0, h, w);
+        tma_load_4d(sbase + kOffQh + kBlk, &tmv, BAR(kVFull), 32, 0, h, w);
+        ++v_issued;
+      }
+      // Never leave with bulk copies in flight (bounded, also after an abort).
+      int no_abort = 0;
+      if (qk_issued > 0)
+        mbar_wait(BAR(kQKFull), (uint32_t)((qk_issued - 1) & 1), &no_abort, p.status, 43, kTimeoutNs);
+      if (v_issued > 0)
+        mbar_wait(BAR(kVFull), (uint32_t)((v_issued - 1) & 1), &no_abort, p.status, 43, kTimeoutNs);
+    }
+  } else if (warp >= 12) {
+    // ---------------- hi / lo split of each landed tile ----------------
+    const int ct = threadIdx.x - 12 * 32;
+    for (int i = 0; i < n_local; ++i) {
+      const uint32_t par = (uint32_t)(i & 1);
+      if (!mbar_wait(BAR(kQKFull), par, abort, p.status, 44, kTimeoutNs)) break;
+      split_blocks(sbase + kOffQh, sbase + kOffQl, 2 * kMat, ct);
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kQKConv));
+      if (!mbar_wait(BAR(kVFull), par, abort, p.status, 45, kTimeoutNs)) break;
+      // V^T of the previous tile is free once its PV products are done.
+      if (!mbar_wait(BAR(kPVDone), par ^ 1u, abort, p.status, 64, kTimeoutNs)) break;
+      split_transpose_v(sbase + kOffQh, sbase + kOffVh, sbase + kOffVl, ct);
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kVConv));
+    }
+  } else if (warp == 1) {
+    // ---------------- UMMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t tS = tmem + kColS, tSR = tmem + kColSR, tO = tmem + kColO, tOR = tmem + kColOR;
+      for (int i = 0; i < n_local; ++i) {
+        const uint32_t par = (uint32_t)(i & 1), prev = par ^ 1u;
+        // S overwrites the P of the previous tile: wait for all of its PV products.
+        if (!mbar_wait(BAR(kQKConv), par, abort, p.status, 46, kTimeoutNs)) break;
+        if (!mbar_wait(BAR(kPVDone), prev, abort, p.status, 47, kTimeoutNs)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (uint32_t)((k >> 2) * kBlk + (k & 3) * 32);
+          const uint64_t bh = desc_sw128(sbase + kOffKh + off, 16, 1024);
+          const uint64_t bl = desc_sw128(sbase + kOffKl + off, 16, 1024);
+          const uint64_t ah = desc_sw128(sbase + kOffQh + off, 16, 1024);
+          const uint64_t al = desc_sw128(sbase + kOffQl + off, 16, 1024);
+          umma_tf32(tS, al, bh, kIdS, k > 0 ? 1u : 0u);
+          umma_tf32(tS, ah, bl, kIdS, 1u);
+          umma_tf32(tS, ah, bh, kIdS, 1u);
+          const uint64_t ah2 = desc_sw128(sbase + kOffQh + off + kRowOff80, 16, 1024);
+          const uint64_t al2 = desc_sw128(sbase + kOffQl + off + kRowOff80, 16, 1024);
+          umma_tf32(tSR, al2, bh, kIdSR, k > 0 ? 1u : 0u);
+          umma_tf32(tSR, ah2, bl, kIdSR, 1u);
+          umma_tf32(tSR, ah2, bh, kIdSR, 1u);
+        }
+        umma_commit(BAR(kSFull));
+        if (!mbar_wait(BAR(kPFull), par, abort, p.status, 48, kTimeoutNs)) break;
+        if (!mbar_wait(BAR(kVConv), par, abort, p.status, 49, kTimeoutNs)) break;
+        if (!mbar_wait(BAR(kOFree), prev, abort, p.status, 50, kTimeoutNs)) break;
+        tc_fence_after();
+        // P_hi products first, then P_lo (written over P_hi).
+#pragma unroll 2
+        for (int j = 0; j < 18; ++j) {
+          const uint64_t vh = vt_desc(sbase + kOffVh, j);
+          const uint64_t vl = vt_desc(sbase + kOffVl, j);
+          umma_tf32_ts(tO, tS + 8 * j, vl, kIdO, j > 0 ? 1u : 0u);
+          umma_tf32_ts(tO, tS + 8 * j, vh, kIdO, 1u);
+        }
+        umma_commit(BAR(kHiDone));
+        if (!mbar_wait(BAR(kPRemHi), par, abort, p.status, 51, kTimeoutNs)) break;
+        if (!mbar_wait(BAR(kORemFree), prev, abort, p.status, 52, kTimeoutNs)) break;
+        tc_fence_after();
+#pragma unroll 2
+        for (int j = 0; j < 18; ++j) {
+          const uint64_t vh = vt_desc(sbase + kOffVh, j);
+          const uint64_t vl = vt_desc(sbase + kOffVl, j);
+          umma_tf32_ts(tOR, tSR + 8 * j, vl, kIdOR, j > 0 ? 1u : 0u);
+          umma_tf32_ts(tOR, tSR + 8 * j, vh, kIdOR, 1u);
+        }
+        umma_commit(BAR(kRemHiDone));
+        if (!mbar_wait(BAR(kPLoFull), par, abort, p.status, 62, kTimeoutNs)) break;
+        tc_fence_after();
+#pragma unroll 2
+        for (int j = 0; j < 18; ++j) {
+          const uint64_t vh = vt_desc(sbase + kOffVh, j);
+          umma_tf32_ts(tO, tS + 8 * j, vh, kIdO, 1u);
+        }
+        umma_commit(BAR(kOFull));
+        if (!mbar_wait(BAR(kPRemLo), par, abort, p.status, 53, kTimeoutNs)) break;
+        tc_fence_after();
+#pragma unroll 2
+        for (int j = 0; j < 18; ++j) {
+          const uint64_t vh = vt_desc(sbase + kOffVh, j);
+          umma_tf32_ts(tOR, tSR + 8 * j, vh, kIdOR, 1u);
+        }
+        umma_commit(BAR(kORemFull));
+        umma_commit(BAR(kPVDone));
+      }
+      umma_commit(BAR(kDone));
+      int no_abort = 0;
+      mbar_wait(BAR(kDone), 0, &no_abort, p.status, 54, kTimeoutNs);
+    }
+  } else if (warp >= 4) {
+    // ---------------- rows 0..127: softmax, P, output rows ----------------
+    const int g = (warp - 4) >> 2;  // key columns 72g .. 72g+71, output columns 32g .. 32g+31
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
+    float* xmax = xchg;        // [2][128]
+    float* xsum = xchg + 256;  // [2][128]
+    int cached_w = -1;
+    uint32_t rel[3] = {0u, 0u, 0u};
+    bool wmask = false;
+    for (int i = 0; i < n_local; ++i) {
+      const int t = t_begin + i, w = t / p.H, h = t - w * p.H;
+      const uint32_t par = (uint32_t)(i & 1);
+      if constexpr (kMask != kNoMask) {
+        if (w != cached_w) {
+          cached_w = w;
+          uint32_t b[5];
+          tc::row_mask_bits<kMask>(p, w % p.nW, row, b);
+          wmask = (b[0] | b[1] | b[2] | b[3] | b[4]) != 0u;
+          const uint32_t w0 = g ? b[2] : b[0], w1 = g ? b[3] : b[1], w2 = g ? b[4] : b[2];
+          const uint32_t w3 = g ? 0u : b[3];
+          const uint32_t sh = g ? 8u : 0u;
+          rel[0] = __funnelshift_r(w0, w1, sh);
+          rel[1] = __funnelshift_r(w1, w2, sh);
+          rel[2] = __funnelshift_r(w2, w3, sh) & 0xffu;
+        }
+      }
+      if (!mbar_wait(BAR(kSFull), par, abort, p.status, 55, kTimeoutNs)) break;
+      tc_fence_after();
+      uint32_t v[72];
+      tc::tmem_ld72(tmem + lane_addr + kColS + 72 * g, v);
+      float pm;
+      if (kMask != kNoMask && wmask) pm = tc::raw_logits72<kMask != kNoMask, kFullN>(v, rel, braw, 72 * g, p.N);
+      else pm = tc::raw_logits72<false, kFullN>(v, rel, braw, 72 * g, p.N);
+      // Each exchange slot is rewritten only after the partner passed the other exchange barrier
+      // of the same tile, so one slot per value suffices.
+      xmax[g * 128 + row] = pm;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kXMax));
+      if (!mbar_wait(BAR(kXMax), par, abort, p.status, 56, kTimeoutNs)) break;
+      const float m = fmaxf(pm, xmax[(g ^ 1) * 128 + row]);
+      const float c = p.scale_log2, mc = -m * c;
+      float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < 72; ++k) {
+        const float e = ex2(fmaf(__uint_as_float(v[k]), c, mc));
+        l4[k & 3] += e;
+        v[k] = __float_as_uint(e);
+      }
+#pragma unroll
+      for (int c8 = 0; c8 < 9; ++c8) {
+        uint32_t hv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) hv[e] = hi_of(v[8 * c8 + e]);
+        tmem_st8(tmem + lane_addr + kColS + 72 * g + 8 * c8, hv);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kPFull));
+      const float pl = (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      xsum[g * 128 + row] = pl;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kXSum));
+      if (!mbar_wait(BAR(kXSum), par, abort, p.status, 57, kTimeoutNs)) break;
+      const float l = pl + xsum[(g ^ 1) * 128 + row];
+      // P_lo over P_hi once the two P_hi products are done.
+      if (!mbar_wait(BAR(kHiDone), par, abort, p.status, 63, kTimeoutNs)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c8 = 0; c8 < 9; ++c8) {
+        uint32_t lv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) lv[e] = lo_of(v[8 * c8 + e]);
+        tmem_st8(tmem + lane_addr + kColS + 72 * g + 8 * c8, lv);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kPLoFull));
+      if (!mbar_wait(BAR(kOFull), par, abort, p.status, 58, kTimeoutNs)) break;
+      tc_fence_after();
+      uint32_t o[32];
+      tmem_ld32(tmem + lane_addr + kColO + 32 * g, o);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kOFree));
+      if (row < p.N) {
+        const float inv = 1.f / l;
+        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (int64_t)w * p.os_w +
+                                                (int64_t)h * p.os_h + (int64_t)row * p.os_n + 32 * g);
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4)
+          dst[c4] = make_float4(__uint_as_float(o[4 * c4]) * inv, __uint_as_float(o[4 * c4 + 1]) * inv,
+                                __uint_as_float(o[4 * c4 + 2]) * inv, __uint_as_float(o[4 * c4 + 3]) * inv);
+      }
+    }
+  } else if (warp == 3) {
+    // ---------------- rows 128..143: M=64 block rows 48..63 ----------------
+    // 16x256b layout: v[4j + {0,1}] = row ra, keys 8j + 2t0 + {0,1}; v[4j + {2,3}] = row rb.
+    const int t0 = lane & 3, t1 = lane >> 2;
+    const int ra = 128 + t1, rb = 136 + t1;
+    const uint32_t lane_s = 96u << 16;
+    int cached_w = -1;
+    uint32_t ta = 0, tb = 0, kp[18];
+    bool wmask = false;
+#pragma unroll
+    for (int j = 0; j < 18; ++j) kp[j] = 0u;
+    for (int i = 0; i < n_local; ++i) {
+      const int t = t_begin + i, w = t / p.H, h = t - w * p.H;
+      const uint32_t par = (uint32_t)(i & 1);
+      if constexpr (kMask != kNoMask) {
+        if (w != cached_w) {
+          cached_w = w;
+          if constexpr (kMask == kGroups) {
+            const uint8_t* gi = p.mask + (int64_t)(w % p.nW) * p.N;
+            ta = ra < p.N ? __ldg(gi + ra) : 0u;
+            tb = rb < p.N ? __ldg(gi + rb) : 0u;
+            uint32_t any = 0;
+#pragma unroll
+            for (int j = 0; j < 18; ++j) {
+              const int key = 8 * j + 2 * t0;
+              const uint32_t lo = key < p.N ? __ldg(gi + key) : ta;
+              const uint32_t hi = key + 1 < p.N ? __ldg(gi + key + 1) : ta;
+              kp[j] = lo | (hi << 8);
+              any |= (lo != ta) | (hi != ta) | (lo != tb) | (hi != tb);
+            }
+            wmask = __any_sync(0xffffffffu, any != 0u);
+          } else {
+            wmask = true;
+          }
+        }
+      }
+      if (!mbar_wait(BAR(kSFull), par, abort, p.status, 59, kTimeoutNs)) break;
+      tc_fence_after();
+      uint32_t v[72];
+      {
+        uint32_t a[64], b[8];
+        tmem_ld_16x256b_r64(tmem + lane_s + kColSR, a);
+        tmem_ld_16x256b_r8(tmem + lane_s + kColSR + 128, b);
+        tmem_wait_ld();
+#pragma unroll
+        for (int k = 0; k < 64; ++k) v[k] = a[k];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[64 + k] = b[k];
+      }
+      float mxa = -INFINITY, mxb = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 18; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = 8 * j + 2 * t0 + e;
+          float ya = __uint_as_float(v[4 * j + e]), yb = __uint_as_float(v[4 * j + 2 + e]);
+          if (kMask != kNoMask && wmask) {
+            if constexpr (kMask == kGroups) {
+              const uint32_t kg = (kp[j] >> (8 * e)) & 0xffu;
+              if (kg != ta) ya += braw;
+              if (kg != tb) yb += braw;
+            } else if constexpr (kMask == kMaskU8) {
+              const uint8_t* mr = p.mask + (int64_t)(w % p.nW) * p.N * p.N;
+              if (key < p.N && ra < p.N && __ldg(mr + (int64_t)ra * p.N + key)) ya += braw;
+              if (key < p.N && rb < p.N && __ldg(mr + (int64_t)rb * p.N + key)) yb += braw;
+            }
+          }
+          if (!kFullN && key >= p.N) {
+            ya = -INFINITY;
+            yb = -INFINITY;
+          }
+          v[4 * j + e] = __float_as_uint(ya);
+          v[4 * j + 2 + e] = __float_as_uint(yb);
+          mxa = fmaxf(mxa, ya);
+          mxb = fmaxf(mxb, yb);
+        }
+      }
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
+      const float c = p.scale_log2, mca = -mxa * c, mcb = -mxb * c;
+      float la = 0.f, lb = 0.f;
+#pragma unroll
+      for (int j = 0; j < 18; ++j) {
+        const float a0 = ex2(fmaf(__uint_as_float(v[4 * j]), c, mca));
+        const float a1 = ex2(fmaf(__uint_as_float(v[4 * j + 1]), c, mca));
+        const float b0 = ex2(fmaf(__uint_as_float(v[4 * j + 2]), c, mcb));
+        const float b1 = ex2(fmaf(__uint_as_float(v[4 * j + 3]), c, mcb));
+        la += a0 + a1;
+        lb += b0 + b1;
+        v[4 * j] = __float_as_uint(a0);
+        v[4 * j + 1] = __float_as_uint(a1);
+        v[4 * j + 2] = __float_as_uint(b0);
+        v[4 * j + 3] = __float_as_uint(b1);
+      }
+      la += __shfl_xor_sync(0xffffffffu, la, 1);
+      la += __shfl_xor_sync(0xffffffffu, la, 2);
+      lb += __shfl_xor_sync(0xffffffffu, lb, 1);
+      lb += __shfl_xor_sync(0xffffffffu, lb, 2);
+      // P_hi over this block's S; P_lo over P_hi once the two P_hi products have run.
+#pragma unroll
+      for (int q = 0; q < 9; ++q) {
+        uint32_t hv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) hv[e] = hi_of(v[8 * q + e]);
+        tmem_st_16x256b_r8(tmem + lane_s + kColSR + 16 * q, hv);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kPRemHi));
+      if (!mbar_wait(BAR(kRemHiDone), par, abort, p.status, 60, kTimeoutNs)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int q = 0; q < 9; ++q) {
+        uint32_t lv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) lv[e] = lo_of(v[8 * q + e]);
+        tmem_st_16x256b_r8(tmem + lane_s + kColSR + 16 * q, lv);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kPRemLo));
+      if (!mbar_wait(BAR(kORemFull), par, abort, p.status, 61, kTimeoutNs)) break;
+      tc_fence_after();
+      uint32_t o[32];
+      tmem_ld_16x256b_r32(tmem + lane_s + kColOR, o);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kORemFree));
+      const float ia = 1.f / la, ib = 1.f / lb;
+      float* base = reinterpret_cast<float*>(p.out) + (int64_t)w * p.os_w + (int64_t)h * p.os_h + 2 * t0;
+      if (ra < p.N) {
+        float2* dst = reinterpret_cast<float2*>(base + (int64_t)ra * p.os_n);
+#pragma unroll
+        for (int jd = 0; jd < 8; ++jd)
+          dst[4 * jd] = make_float2(__uint_as_float(o[4 * jd]) * ia, __uint_as_float(o[4 * jd + 1]) * ia);
+      }
+      if (rb < p.N) {
+        float2* dst = reinterpret_cast<float2*>(base + (int64_t)rb * p.os_n);
+#pragma unroll
+        for (int jd = 0; jd < 8; ++jd)
+          dst[4 * jd] = make_float2(__uint_as_float(o[4 * jd + 2]) * ib, __uint_as_float(o[4 * jd + 3]) * ib);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace tc32
+
+// ------------------------------------------------------------------------------------------
 // Host side
 // ------------------------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
@@ -1308,6 +1841,16 @@ int launch_tc_bf16(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorM
   return check_launch("attn_tc_bf16_kernel");
 }
 
+template <int kMask>
+int launch_tc_tf32(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p,
+                   cudaStream_t s) {
+  auto kern = p.N == kMaxN ? tc32::attn_tc_tf32_kernel<kMask, true> : tc32::attn_tc_tf32_kernel<kMask, false>;
+  FA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tc32::kSmem));
+  const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
+  kern<<<grid, tc32::kThreads, tc32::kSmem, s>>>(mq, mk, mv, p);
+  return check_launch("attn_tc_tf32_kernel");
+}
+
 template <bool kF32, int kMask>
 int launch_sync(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Params& p,
                 cudaStream_t s) {
@@ -1323,6 +1866,13 @@ int launch_sync(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
 // the tensor-memory kernel); the default is the tcgen05 kernel.
 bool use_sync_bf16() {
   const char* e = getenv("FA_ATTN_BF16_KERNEL");
+  return e && std::string(e) == "mma_sync";
+}
+
+// FA_ATTN_FP32_KERNEL=mma_sync selects the warp-level 3xTF32 kernel for fp32 I/O (a cross-check of
+// the tcgen05 kernel, same accuracy); the default is the tcgen05 kernel.
+bool use_sync_fp32() {
+  const char* e = getenv("FA_ATTN_FP32_KERNEL");
   return e && std::string(e) == "mma_sync";
 }
 
@@ -1378,6 +1928,13 @@ int run(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const voi
   cudaStream_t s = (cudaStream_t)stream;
   const int kind = mask_u8 ? kMaskU8 : (group_ids ? kGroups : kNoMask);
   if (f32) {
+    // The tcgen05 kernel writes 16-byte output vectors: needs 16-byte aligned rows.
+    const bool out16f = aligned16(out) && p.os_w % 4 == 0 && p.os_h % 4 == 0 && p.os_n % 4 == 0;
+    if (!use_sync_fp32() && out16f) {
+      if (kind == kGroups) return launch_tc_tf32<kGroups>(mq, mk, mv, p, s);
+      if (kind == kMaskU8) return launch_tc_tf32<kMaskU8>(mq, mk, mv, p, s);
+      return launch_tc_tf32<kNoMask>(mq, mk, mv, p, s);
+    }
     if (kind == kGroups) return launch_sync<true, kGroups>(mq, mk, mv, p, s);
     if (kind == kMaskU8) return launch_sync<true, kMaskU8>(mq, mk, mv, p, s);
     return launch_sync<true, kNoMask>(mq, mk, mv, p, s);

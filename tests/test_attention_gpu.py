@@ -235,3 +235,36 @@ def test_region_fit_flag_fast_path_and_broken_promise():
     _lib.check(lib.fa_attention_status(ctypes.byref(st)), "status")
     assert st.value == 28
     _lib.check(lib.fa_attention_status_reset(None), "status reset")
+
+
+@pytest.mark.parametrize("mask", ["none", "bias", "groups"])
+@pytest.mark.parametrize("N", [144, 130, 96])
+def test_fp32_tensor_memory_kernel_matches_warp_mma_kernel(monkeypatch, mask, N):
+    """FP32 I/O: the tcgen05 3xTF32 kernel (default) and the warp-level 3xTF32 kernel
+    (FA_ATTN_FP32_KERNEL=mma_sync) both stay within the FP32-tier bound of strict FP64 attention.
+    720 (window, head) tiles, so every CTA runs several tiles through its pipeline."""
+    Bwin, H, nW = 90, 8, 6
+    q, k, v = _qkv(Bwin, H, N, 64, seed=13, scale=0.5)
+    g = torch.Generator().manual_seed(N)
+    ids = torch.randint(0, 5, (nW, N), generator=g).to(torch.uint8)
+    ids[0] = 2  # one region: nothing masked in this window
+    bias = None
+    kw = {}
+    if mask == "bias":
+        bias = _half_bias(nW, N)
+        kw["bias"] = bias.cuda()
+    elif mask == "groups":
+        bias = torch.where(ids[:, :, None] != ids[:, None, :], -100.0, 0.0)
+        kw["group_ids"] = ids.cuda()
+    qc, kc, vc = q.cuda(), k.cuda(), v.cuda()
+    a = fa.window_attn_fwd_cute(qc, kc, vc, precision=P.TF32_ACC_FP32, **kw)
+    monkeypatch.setenv("FA_ATTN_FP32_KERNEL", "mma_sync")
+    b = fa.window_attn_fwd_cute(qc, kc, vc, precision=P.TF32_ACC_FP32, **kw)
+    monkeypatch.delenv("FA_ATTN_FP32_KERNEL")
+    ref = OB.window_attention_core(q.double(), k.double(), v.double(),
+                                   bias.double() if bias is not None else None)
+    for out in (a, b):
+        assert out.dtype == torch.float32
+        assert _rel_l2(out, ref) <= 1e-5
+        assert (out.cpu().double() - ref).abs().max().item() <= 2e-5
+    assert (a - b).abs().max().item() <= 2e-5
