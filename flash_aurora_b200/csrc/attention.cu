@@ -1271,8 +1271,9 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
 // One (window, head) tile at a time per CTA, single-buffered: shared memory holds hi and lo of
 // Q and K (144 x 32-float blocks with 128-byte swizzle, as TMA writes them) and of V^T. kind::tf32
 // takes K-major operands only (an MN-major tf32 operand yields zeros on B200), so V, which TMA
-// lands in the Q slot once the S products are done, is transposed by the split warps into
-// 64 x 144 K-major blocks: keys 0..127 with 128-byte swizzle, keys 128..143 with 32-byte swizzle.
+// lands in the V^T lo slot as soon as the previous tile's PV products are done, is transposed in
+// registers by the split warps into 64 x 144 K-major blocks: keys 0..127 with 128-byte swizzle,
+// keys 128..143 with 32-byte swizzle.
 //   S  = Q K^T  rows 0..127 (M=128) and rows 80..143 (M=64), N=144, 8 K-steps x 3 products, both
 //               operands K-major in shared memory;
 //   P           the softmax warps write P_hi over S in TMEM (tcgen05.st), then P_lo over P_hi once
@@ -1283,9 +1284,12 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
 // The issuer interleaves the two blocks, so that each block's P_lo store overlaps the other block's
 // products. TMEM columns: S / P 0..143, O 160..223, M=64 block S / P 224..367 and O 384..447.
 // Warp roles (512 threads, one CTA per SM, a contiguous range of tiles per CTA):
-//   warp 0       TMA: Q and K of a tile once V of the previous one is transposed, V once its S
-//                products are done;
-//   warp 1       TMEM owner and UMMA issuer (one thread, blocking on each input);
+//   warp 0       TMA: Q and K of a tile once the previous tile's S products are done, V once its
+//                PV products are done;
+//   warp 1       TMEM owner and UMMA issuer (one thread, blocking on each input). A tf32 UMMA
+//                costs about 74 cycles at N=144 and has a floor near 48 cycles at N=64, so the
+//                issue sequence is unrolled with precomputed descriptors, and the M=128 S block is
+//                committed before the M=64 one so that the softmax overlaps the latter;
 //   warp 3       rows 128..143 (16x256b TMEM shape, two rows per thread, quad reductions);
 //   warps 4..11  rows 0..127: two warpgroups of 72 keys per row (row max / sum exchanged through
 //                shared memory), then the output rows (32 columns per warpgroup);
@@ -1297,7 +1301,7 @@ namespace tc32 {
 constexpr int kBlk = kTileBytes;  // 144 rows x 32 floats (128 bytes)
 constexpr int kMat = 2 * kBlk;    // one 144 x 64 fp32 operand
 // Raw / hi blocks of Q and K are adjacent, and so are their lo blocks: one split pass covers both.
-// V lands in the Q slot (kOffQh); its transposed hi and lo go to kOffVh / kOffVl.
+// V lands in the V^T lo slot (kOffVl); its transposed hi and lo go to kOffVh / kOffVl.
 constexpr int kOffQh = 0, kOffKh = kMat, kOffQl = 2 * kMat, kOffKl = 3 * kMat, kOffVh = 4 * kMat, kOffVl = 5 * kMat;
 // V^T (64 rows of head dims): keys 32b..32b+31 in 128-byte-swizzled blocks b = 0..3 (8 KB each),
 // keys 128..135 and 136..143 in 32-byte-swizzled blocks (2 KB each); kMat bytes in all.
@@ -1309,8 +1313,8 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 160, kColSR = 224, kColOR = 384;
 constexpr uint32_t kRowOff80 = 80 * 128;
 constexpr uint32_t kHiMask = 0xFFFFE000u;     // sign, exponent and the 10 mantissa bits of tf32
-enum { kQKFull = 0, kQKConv, kVFull, kVConv, kSFull, kPFull, kHiDone, kPLoFull, kPRemHi, kRemHiDone, kPRemLo,
-       kOFull, kOFree, kORemFull, kORemFree, kPVDone, kXMax, kXSum, kDone, kNumBars };
+enum { kQKFull = 0, kQKConv, kVFull, kVRead, kVConv, kSFull, kSRemFull, kPFull, kHiDone, kPLoFull, kPRemHi,
+       kRemHiDone, kPRemLo, kOFull, kOFree, kORemFull, kORemFree, kPVDone, kXMax, kXSum, kDone, kNumBars };
 constexpr int kSmem = 6 * kMat + kXchgBytes + kNumBars * 8 + 16 + 1024;
 static_assert(kSmem <= 227 * 1024, "shared memory budget");
 constexpr uint32_t kIdS = ptx::make_idesc(2, 128, kMaxN, false, false);
@@ -1331,33 +1335,11 @@ __device__ __forceinline__ uint32_t vt_off(int d, int key) {
   return (uint32_t)(kVtSw32 + (k2 >> 3) * 2048 + d * 32 + ((((k2 & 7) >> 2) ^ ((d >> 2) & 1)) << 4));
 }
 
-// B operand descriptor of PV K-step j (keys 8j..8j+7) in a V^T buffer.
-__device__ __forceinline__ uint64_t vt_desc(uint32_t vt, int j) {
-  return j < 16 ? desc_sw128(vt + (uint32_t)((j >> 2) * 8192 + (j & 3) * 32), 16, 1024)
-                : desc_sw32(vt + (uint32_t)(kVtSw32 + (j - 16) * 2048), 256);
-}
-
-// V (144 keys x 64 dims as TMA wrote it at `raw`) -> hi and lo of V^T. Each thread moves 4 x 4
-// blocks (4 keys x 4 dims); blocks are enumerated along diagonals so that the eight threads of a
-// quarter warp touch eight different 16-byte columns on both sides.
-__device__ __forceinline__ void split_transpose_v(uint32_t raw, uint32_t vh, uint32_t vl, int ct) {
-#pragma unroll 1
-  for (int n = ct; n < 36 * 16; n += kConvThreads) {
-    const int dc = n & 15, kg = ((n >> 4) + dc) % 36;
-    uint32_t x[4][4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int key = 4 * kg + r;
-      ld_shared_v4(raw + (uint32_t)((dc >> 3) * kBlk + key * 128 + (((dc & 7) ^ (key & 7)) << 4)), x[r][0], x[r][1],
-                   x[r][2], x[r][3]);
-    }
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t o = vt_off(4 * dc + c, 4 * kg);
-      st_shared_v4(vh + o, hi_of(x[0][c]), hi_of(x[1][c]), hi_of(x[2][c]), hi_of(x[3][c]));
-      st_shared_v4(vl + o, lo_of(x[0][c]), lo_of(x[1][c]), lo_of(x[2][c]), lo_of(x[3][c]));
-    }
-  }
+// B operand descriptor of PV K-step j (keys 8j..8j+7) of a V^T buffer, from the descriptors of its
+// first 128-byte-swizzled block (d128) and first 32-byte-swizzled block (d32): the start address
+// field counts 16-byte units, so moving inside the buffer adds offset / 16.
+__device__ __forceinline__ uint64_t vt_desc(uint64_t d128, uint64_t d32, int j) {
+  return j < 16 ? d128 + (uint64_t)(((j >> 2) * 8192 + (j & 3) * 32) >> 4) : d32 + (uint64_t)(((j - 16) * 2048) >> 4);
 }
 
 // hi (in place) and lo of `bytes` of landed operand blocks; 16 bytes per thread and step.
@@ -1393,7 +1375,7 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
   if (threadIdx.x == 0) {
     abort_flag = 0;
     for (int b = 0; b < kNumBars; ++b) {
-      const uint32_t count = (b == kQKConv || b == kVConv) ? 4u
+      const uint32_t count = (b == kQKConv || b == kVRead || b == kVConv) ? 4u
                              : (b == kPFull || b == kPLoFull || b == kOFree || b == kXMax || b == kXSum) ? 8u
                                                                                                            : 1u;
       mbar_init(BAR(b), count);
@@ -1421,18 +1403,17 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       for (int i = 0; i < n_local; ++i) {
         const int t = t_begin + i, w = t / p.H, h = t - w * p.H;
         const uint32_t prev = (uint32_t)((i & 1) ^ 1);  // completion of tile i-1 (free on tile 0)
-        // The Q slot holds V of tile i-1 until it is transposed (which follows its S products).
-        if (!mbar_wait(BAR(kVConv), prev, abort, p.status, 41, kTimeoutNs)) break;
+        if (!mbar_wait(BAR(kSRemFull), prev, abort, p.status, 41, kTimeoutNs)) break;
         mbar_arrive_expect_tx(BAR(kQKFull), 2 * kMat);
         tma_load_4d(sbase + kOffQh, &tmq, BAR(kQKFull), 0, 0, h, w);
         tma_load_4d(sbase + kOffQh + kBlk, &tmq, BAR(kQKFull), 32, 0, h, w);
         tma_load_4d(sbase + kOffKh, &tmk, BAR(kQKFull), 0, 0, h, w);
         tma_load_4d(sbase + kOffKh + kBlk, &tmk, BAR(kQKFull), 32, 0, h, w);
         ++qk_issued;
-        if (!mbar_wait(BAR(kSFull), (uint32_t)(i & 1), abort, p.status, 42, kTimeoutNs)) break;
+        if (!mbar_wait(BAR(kPVDone), prev, abort, p.status, 42, kTimeoutNs)) break;
         mbar_arrive_expect_tx(BAR(kVFull), kMat);
-        tma_load_4d(sbase + kOffQh, &tmv, BAR(kVFull), 0, 0, h, w);
-        tma_load_4d(sbase + kOffQh + kBlk, &tmv, BAR(kVFull), 32, 0, h, w);
+        tma_load_4d(sbase + kOffVl, &tmv, BAR(kVFull), 0, 0, h, w);
+        tma_load_4d(sbase + kOffVl + kBlk, &tmv, BAR(kVFull), 32, 0, h, w);
         ++v_issued;
       }
       // Never leave with bulk copies in flight (bounded, also after an abort).
@@ -1452,10 +1433,41 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kQKConv));
+      // V landed in the lo slot after the previous tile's PV products (so both V^T slots are
+      // free): read this thread's 4 x 4 blocks (4 keys x 4 dims), wait until every split warp has
+      // read, then write them transposed. Blocks run along diagonals, so the eight threads of a
+      // quarter warp touch eight different 16-byte columns on both sides.
       if (!mbar_wait(BAR(kVFull), par, abort, p.status, 45, kTimeoutNs)) break;
-      // V^T of the previous tile is free once its PV products are done.
-      if (!mbar_wait(BAR(kPVDone), par ^ 1u, abort, p.status, 64, kTimeoutNs)) break;
-      split_transpose_v(sbase + kOffQh, sbase + kOffVh, sbase + kOffVl, ct);
+      uint32_t x[5][4][4];
+#pragma unroll
+      for (int m = 0; m < 5; ++m) {
+        const int n = ct + kConvThreads * m;
+        if (n < 36 * 16) {
+          const int dc = n & 15, kg = ((n >> 4) + dc) % 36;
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int key = 4 * kg + r;
+            ld_shared_v4(sbase + kOffVl + (uint32_t)((dc >> 3) * kBlk + key * 128 + (((dc & 7) ^ (key & 7)) << 4)),
+                         x[m][r][0], x[m][r][1], x[m][r][2], x[m][r][3]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(kVRead));
+      if (!mbar_wait(BAR(kVRead), par, abort, p.status, 64, kTimeoutNs)) break;
+#pragma unroll
+      for (int m = 0; m < 5; ++m) {
+        const int n = ct + kConvThreads * m;
+        if (n < 36 * 16) {
+          const int dc = n & 15, kg = ((n >> 4) + dc) % 36;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t o = vt_off(4 * dc + c, 4 * kg);
+            st_shared_v4(sbase + kOffVh + o, hi_of(x[m][0][c]), hi_of(x[m][1][c]), hi_of(x[m][2][c]), hi_of(x[m][3][c]));
+            st_shared_v4(sbase + kOffVl + o, lo_of(x[m][0][c]), lo_of(x[m][1][c]), lo_of(x[m][2][c]), lo_of(x[m][3][c]));
+          }
+        }
+      }
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kVConv));
@@ -1464,6 +1476,10 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
     // ---------------- UMMA issuer ----------------
     if (lane == 0) {
       const uint32_t tS = tmem + kColS, tSR = tmem + kColSR, tO = tmem + kColO, tOR = tmem + kColOR;
+      const uint64_t dQh = desc_sw128(sbase + kOffQh, 16, 1024), dQl = desc_sw128(sbase + kOffQl, 16, 1024);
+      const uint64_t dKh = desc_sw128(sbase + kOffKh, 16, 1024), dKl = desc_sw128(sbase + kOffKl, 16, 1024);
+      const uint64_t dVh = desc_sw128(sbase + kOffVh, 16, 1024), dVl = desc_sw128(sbase + kOffVl, 16, 1024);
+      const uint64_t dVh32 = desc_sw32(sbase + kOffVh + kVtSw32, 256), dVl32 = desc_sw32(sbase + kOffVl + kVtSw32, 256);
       for (int i = 0; i < n_local; ++i) {
         const uint32_t par = (uint32_t)(i & 1), prev = par ^ 1u;
         // S overwrites the P of the previous tile: wait for all of its PV products.
@@ -1472,30 +1488,29 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const uint32_t off = (uint32_t)((k >> 2) * kBlk + (k & 3) * 32);
-          const uint64_t bh = desc_sw128(sbase + kOffKh + off, 16, 1024);
-          const uint64_t bl = desc_sw128(sbase + kOffKl + off, 16, 1024);
-          const uint64_t ah = desc_sw128(sbase + kOffQh + off, 16, 1024);
-          const uint64_t al = desc_sw128(sbase + kOffQl + off, 16, 1024);
-          umma_tf32(tS, al, bh, kIdS, k > 0 ? 1u : 0u);
-          umma_tf32(tS, ah, bl, kIdS, 1u);
-          umma_tf32(tS, ah, bh, kIdS, 1u);
-          const uint64_t ah2 = desc_sw128(sbase + kOffQh + off + kRowOff80, 16, 1024);
-          const uint64_t al2 = desc_sw128(sbase + kOffQl + off + kRowOff80, 16, 1024);
-          umma_tf32(tSR, al2, bh, kIdSR, k > 0 ? 1u : 0u);
-          umma_tf32(tSR, ah2, bl, kIdSR, 1u);
-          umma_tf32(tSR, ah2, bh, kIdSR, 1u);
+          const uint64_t off = (uint64_t)(((k >> 2) * kBlk + (k & 3) * 32) >> 4);
+          umma_tf32(tS, dQl + off, dKh + off, kIdS, k > 0 ? 1u : 0u);
+          umma_tf32(tS, dQh + off, dKl + off, kIdS, 1u);
+          umma_tf32(tS, dQh + off, dKh + off, kIdS, 1u);
         }
         umma_commit(BAR(kSFull));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint64_t off = (uint64_t)(((k >> 2) * kBlk + (k & 3) * 32) >> 4), a80 = kRowOff80 >> 4;
+          umma_tf32(tSR, dQl + off + a80, dKh + off, kIdSR, k > 0 ? 1u : 0u);
+          umma_tf32(tSR, dQh + off + a80, dKl + off, kIdSR, 1u);
+          umma_tf32(tSR, dQh + off + a80, dKh + off, kIdSR, 1u);
+        }
+        umma_commit(BAR(kSRemFull));
         if (!mbar_wait(BAR(kPFull), par, abort, p.status, 48, kTimeoutNs)) break;
         if (!mbar_wait(BAR(kVConv), par, abort, p.status, 49, kTimeoutNs)) break;
         if (!mbar_wait(BAR(kOFree), prev, abort, p.status, 50, kTimeoutNs)) break;
         tc_fence_after();
         // P_hi products first, then P_lo (written over P_hi).
-#pragma unroll 2
+#pragma unroll
         for (int j = 0; j < 18; ++j) {
-          const uint64_t vh = vt_desc(sbase + kOffVh, j);
-          const uint64_t vl = vt_desc(sbase + kOffVl, j);
+          const uint64_t vh = vt_desc(dVh, dVh32, j);
+          const uint64_t vl = vt_desc(dVl, dVl32, j);
           umma_tf32_ts(tO, tS + 8 * j, vl, kIdO, j > 0 ? 1u : 0u);
           umma_tf32_ts(tO, tS + 8 * j, vh, kIdO, 1u);
         }
@@ -1503,27 +1518,27 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
         if (!mbar_wait(BAR(kPRemHi), par, abort, p.status, 51, kTimeoutNs)) break;
         if (!mbar_wait(BAR(kORemFree), prev, abort, p.status, 52, kTimeoutNs)) break;
         tc_fence_after();
-#pragma unroll 2
+#pragma unroll
         for (int j = 0; j < 18; ++j) {
-          const uint64_t vh = vt_desc(sbase + kOffVh, j);
-          const uint64_t vl = vt_desc(sbase + kOffVl, j);
+          const uint64_t vh = vt_desc(dVh, dVh32, j);
+          const uint64_t vl = vt_desc(dVl, dVl32, j);
           umma_tf32_ts(tOR, tSR + 8 * j, vl, kIdOR, j > 0 ? 1u : 0u);
           umma_tf32_ts(tOR, tSR + 8 * j, vh, kIdOR, 1u);
         }
         umma_commit(BAR(kRemHiDone));
         if (!mbar_wait(BAR(kPLoFull), par, abort, p.status, 62, kTimeoutNs)) break;
         tc_fence_after();
-#pragma unroll 2
+#pragma unroll
         for (int j = 0; j < 18; ++j) {
-          const uint64_t vh = vt_desc(sbase + kOffVh, j);
+          const uint64_t vh = vt_desc(dVh, dVh32, j);
           umma_tf32_ts(tO, tS + 8 * j, vh, kIdO, 1u);
         }
         umma_commit(BAR(kOFull));
         if (!mbar_wait(BAR(kPRemLo), par, abort, p.status, 53, kTimeoutNs)) break;
         tc_fence_after();
-#pragma unroll 2
+#pragma unroll
         for (int j = 0; j < 18; ++j) {
-          const uint64_t vh = vt_desc(sbase + kOffVh, j);
+          const uint64_t vh = vt_desc(dVh, dVh32, j);
           umma_tf32_ts(tOR, tSR + 8 * j, vh, kIdOR, 1u);
         }
         umma_commit(BAR(kORemFull));
@@ -1668,7 +1683,7 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
           }
         }
       }
-      if (!mbar_wait(BAR(kSFull), par, abort, p.status, 59, kTimeoutNs)) break;
+      if (!mbar_wait(BAR(kSRemFull), par, abort, p.status, 59, kTimeoutNs)) break;
       tc_fence_after();
       uint32_t v[72];
       {
