@@ -1261,9 +1261,9 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
 // ------------------------------------------------------------------------------------------
 // FP32 I/O kernel on the 5th-generation tensor cores: 3xTF32 with tcgen05.mma kind::tf32.
 //
-// Every operand x is split as x = hi + lo: hi is x with its 13 low mantissa bits cleared (a tf32
-// value, so the tensor core takes it exactly), lo = x - hi (exact in fp32; the tensor core rounds
-// it to tf32). A product a.b accumulates a_lo.b_hi + a_hi.b_lo + a_hi.b_hi in fp32; the dropped
+// Every operand x is split as x = hi + lo: hi is x with its 13 low mantissa bits cleared, lo = x - hi
+// (exact in fp32). kind::tf32 truncates its fp32 inputs to tf32 (measured on B200: 1 + 3*2^-12 is
+// taken as 1), so x itself serves as hi and only lo is stored; the tensor core truncates lo too. A product a.b accumulates a_lo.b_hi + a_hi.b_lo + a_hi.b_hi in fp32; the dropped
 // a_lo.b_lo term and the rounding of lo leave it within about 2^-21 of the fp32 product, the
 // accuracy of the warp-level 3xTF32 kernel above, unlike the upstream 1xTF32 QK^T + BF16 PV
 // kernel (ops/cute/_kernel_fp32.py:491-493).
@@ -1279,10 +1279,12 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
 //   P           the softmax warps write P_hi over S in TMEM (tcgen05.st), then P_lo over P_hi once
 //               the two P_hi products have run;
 //   O  = P V    M=128, N=64, 18 K-steps x 3 products, A (P) from TMEM, V^T in shared memory.
-// A TMEM A operand must sit in the same lanes as its accumulator, so the M=64 block (rows 128..143
-// are its rows 48..63) keeps S, P and O in the first lane half (lanes 0-15 of each 32-lane group).
-// The issuer interleaves the two blocks, so that each block's P_lo store overlaps the other block's
-// products. TMEM columns: S / P 0..143, O 160..223, M=64 block S / P 224..367 and O 384..447.
+// A TMEM A operand must sit in the same lanes as its accumulator. The M=64 block (rows 128..143 are
+// its rows 48..63) fills half of the lanes: its S and P_hi use the first lane half (lanes 0-15 of
+// each 32-lane group) of columns 224..367 with their O accumulator in the first lane half of
+// 384..447, and its P_lo uses the second lane half of the same columns with a second O accumulator
+// there; the epilogue adds the two. Its products therefore run in one go, while the softmax warps
+// write the M=128 block's P_lo. TMEM columns: S / P 0..143, O 160..223, M=64 block 224..447.
 // Warp roles (512 threads, one CTA per SM, a contiguous range of tiles per CTA):
 //   warp 0       TMA: Q and K of a tile once the previous tile's S products are done, V once its
 //                PV products are done;
@@ -1293,7 +1295,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
 //   warp 3       rows 128..143 (16x256b TMEM shape, two rows per thread, quad reductions);
 //   warps 4..11  rows 0..127: two warpgroups of 72 keys per row (row max / sum exchanged through
 //                shared memory), then the output rows (32 columns per warpgroup);
-//   warps 12..15 split Q and K into hi (in place) and lo; transpose and split V.
+//   warps 12..15 write the lo parts of Q and K; transpose V into its hi and lo parts.
 // Every wait is bounded (status word + abort flag); warp 2 only takes part in the set-up.
 // ------------------------------------------------------------------------------------------
 namespace tc32 {
@@ -1311,10 +1313,11 @@ constexpr int kThreads = 512;
 constexpr int kConvThreads = 128;             // warps 12..15
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 160, kColSR = 224, kColOR = 384;
+constexpr uint32_t kLaneHalf = 16u << 16;  // second lane half of an M=64 block
 constexpr uint32_t kRowOff80 = 80 * 128;
 constexpr uint32_t kHiMask = 0xFFFFE000u;     // sign, exponent and the 10 mantissa bits of tf32
-enum { kQKFull = 0, kQKConv, kVFull, kVRead, kVConv, kSFull, kSRemFull, kPFull, kHiDone, kPLoFull, kPRemHi,
-       kRemHiDone, kPRemLo, kOFull, kOFree, kORemFull, kORemFree, kPVDone, kXMax, kXSum, kDone, kNumBars };
+enum { kQKFull = 0, kQKConv, kVFull, kVRead, kVConv, kSFull, kSRemFull, kPFull, kHiDone, kPLoFull, kPRemFull,
+       kOFull, kOFree, kORemFull, kORemFree, kPVDone, kXMax, kXSum, kDone, kNumBars };
 constexpr int kSmem = 6 * kMat + kXchgBytes + kNumBars * 8 + 16 + 1024;
 static_assert(kSmem <= 227 * 1024, "shared memory budget");
 constexpr uint32_t kIdS = ptx::make_idesc(2, 128, kMaxN, false, false);
@@ -1342,13 +1345,13 @@ __device__ __forceinline__ uint64_t vt_desc(uint64_t d128, uint64_t d32, int j) 
   return j < 16 ? d128 + (uint64_t)(((j >> 2) * 8192 + (j & 3) * 32) >> 4) : d32 + (uint64_t)(((j - 16) * 2048) >> 4);
 }
 
-// hi (in place) and lo of `bytes` of landed operand blocks; 16 bytes per thread and step.
-__device__ __forceinline__ void split_blocks(uint32_t hi, uint32_t lo, int bytes, int ct) {
+// lo of `bytes` of landed operand blocks (the landed values are their own hi); 16 bytes per
+// thread and step.
+__device__ __forceinline__ void split_blocks(uint32_t raw, uint32_t lo, int bytes, int ct) {
 #pragma unroll 4
   for (int o = ct * 16; o < bytes; o += kConvThreads * 16) {
     uint32_t a, b, c, d;
-    ld_shared_v4(hi + (uint32_t)o, a, b, c, d);
-    st_shared_v4(hi + (uint32_t)o, hi_of(a), hi_of(b), hi_of(c), hi_of(d));
+    ld_shared_v4(raw + (uint32_t)o, a, b, c, d);
     st_shared_v4(lo + (uint32_t)o, lo_of(a), lo_of(b), lo_of(c), lo_of(d));
   }
 }
@@ -1515,7 +1518,8 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
           umma_tf32_ts(tO, tS + 8 * j, vh, kIdO, 1u);
         }
         umma_commit(BAR(kHiDone));
-        if (!mbar_wait(BAR(kPRemHi), par, abort, p.status, 51, kTimeoutNs)) break;
+        // M=64 block: P_hi (first lane half) and P_lo (second lane half), one O accumulator each.
+        if (!mbar_wait(BAR(kPRemFull), par, abort, p.status, 51, kTimeoutNs)) break;
         if (!mbar_wait(BAR(kORemFree), prev, abort, p.status, 52, kTimeoutNs)) break;
         tc_fence_after();
 #pragma unroll
@@ -1524,8 +1528,9 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
           const uint64_t vl = vt_desc(dVl, dVl32, j);
           umma_tf32_ts(tOR, tSR + 8 * j, vl, kIdOR, j > 0 ? 1u : 0u);
           umma_tf32_ts(tOR, tSR + 8 * j, vh, kIdOR, 1u);
+          umma_tf32_ts(tOR + kLaneHalf, tSR + kLaneHalf + 8 * j, vh, kIdOR, j > 0 ? 1u : 0u);
         }
-        umma_commit(BAR(kRemHiDone));
+        umma_commit(BAR(kORemFull));
         if (!mbar_wait(BAR(kPLoFull), par, abort, p.status, 62, kTimeoutNs)) break;
         tc_fence_after();
 #pragma unroll
@@ -1534,14 +1539,6 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
           umma_tf32_ts(tO, tS + 8 * j, vh, kIdO, 1u);
         }
         umma_commit(BAR(kOFull));
-        if (!mbar_wait(BAR(kPRemLo), par, abort, p.status, 53, kTimeoutNs)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int j = 0; j < 18; ++j) {
-          const uint64_t vh = vt_desc(dVh, dVh32, j);
-          umma_tf32_ts(tOR, tSR + 8 * j, vh, kIdOR, 1u);
-        }
-        umma_commit(BAR(kORemFull));
         umma_commit(BAR(kPVDone));
       }
       umma_commit(BAR(kDone));
@@ -1747,36 +1744,30 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       la += __shfl_xor_sync(0xffffffffu, la, 2);
       lb += __shfl_xor_sync(0xffffffffu, lb, 1);
       lb += __shfl_xor_sync(0xffffffffu, lb, 2);
-      // P_hi over this block's S; P_lo over P_hi once the two P_hi products have run.
+      // P_hi over this block's S (first lane half), P_lo in the second lane half.
 #pragma unroll
       for (int q = 0; q < 9; ++q) {
-        uint32_t hv[8];
+        uint32_t hv[8], lv[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) hv[e] = hi_of(v[8 * q + e]);
+        for (int e = 0; e < 8; ++e) {
+          hv[e] = hi_of(v[8 * q + e]);
+          lv[e] = lo_of(v[8 * q + e]);
+        }
         tmem_st_16x256b_r8(tmem + lane_s + kColSR + 16 * q, hv);
+        tmem_st_16x256b_r8(tmem + lane_s + kLaneHalf + kColSR + 16 * q, lv);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kPRemHi));
-      if (!mbar_wait(BAR(kRemHiDone), par, abort, p.status, 60, kTimeoutNs)) break;
-      tc_fence_after();
-#pragma unroll
-      for (int q = 0; q < 9; ++q) {
-        uint32_t lv[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) lv[e] = lo_of(v[8 * q + e]);
-        tmem_st_16x256b_r8(tmem + lane_s + kColSR + 16 * q, lv);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kPRemLo));
+      if (lane == 0) mbar_arrive(BAR(kPRemFull));
       if (!mbar_wait(BAR(kORemFull), par, abort, p.status, 61, kTimeoutNs)) break;
       tc_fence_after();
-      uint32_t o[32];
+      uint32_t o[32], o2[32];
       tmem_ld_16x256b_r32(tmem + lane_s + kColOR, o);
+      tmem_ld_16x256b_r32(tmem + lane_s + kLaneHalf + kColOR, o2);
       tmem_wait_ld();
+#pragma unroll
+      for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) + __uint_as_float(o2[k]));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kORemFree));
