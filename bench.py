@@ -484,6 +484,17 @@ def run_layout_adaln(args) -> None:
                   lambda: fa.gelu_erf(h, inplace=True, method="erff"), h.numel() * 2 * 2))
     cases.append(("[torch F.gelu on the same tensor, for comparison]",
                   lambda: torch.nn.functional.gelu(h), h.numel() * 2 * 2))
+    # The Perceiver level decoder's post-norm LayerNorm + residual at the era5 latent shape
+    # (B*H*W = 259200 latents x 13 pressure levels, D = 512), bf16: x + residual read, out written.
+    lat = torch.randn(259200, 13, 512, device=dev, generator=g).bfloat16()
+    lat_res = torch.randn(259200, 13, 512, device=dev, generator=g).bfloat16()
+    lw = torch.randn(512, device=dev, generator=g) * 0.1 + 1.0
+    lb = torch.randn(512, device=dev, generator=g) * 0.1
+    cases.append(("perceiver LayerNorm + residual, decoder latents (259200, 13, 512) bf16",
+                  lambda: fa.layernorm_affine_add_residual_forward(lat, lat_res, lw, lb, 1e-5), lat.numel() * 2 * 3))
+    cases.append(("[torch layer_norm + add on the same tensors, for comparison]",
+                  lambda: torch.nn.functional.layer_norm(lat, (512,), lw.bfloat16(), lb.bfloat16(), 1e-5) + lat_res,
+                  lat.numel() * 2 * 3))
     for name, fn, nbytes in cases:
         ms = _time_launches(fn, args.steps, flush=flush)
         gbs = nbytes / (ms * 1e-3) / 1e9
@@ -493,7 +504,7 @@ def run_layout_adaln(args) -> None:
               flush=True)
     # The block MLP's fc1 + GELU at each stage of config 4: fused tensor-core kernel vs cuBLAS + GELU.
     _, tf_peak, _ = _peaks()
-    del h
+    del h, lat, lat_res
     for tag, M, K, N in (("S1", 259200, 512, 2048), ("S2", 64800, 1024, 4096), ("S3", 16200, 2048, 8192)):
         a = torch.randn(M, K, device=dev, generator=g).bfloat16()
         w = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()

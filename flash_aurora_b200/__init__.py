@@ -17,6 +17,7 @@ PyTorch host layer that mirrors the operator interface of upstream Flash-Aurora:
 
 from .activation import gelu_erf
 from .linear import linear_bias_act
+from .perceiver_ln import layernorm_affine_add_residual_forward, layernorm_affine_forward
 from .adaln import (
     adaptive_layernorm_film_add_residual_forward,
     adaptive_layernorm_film_forward,
@@ -46,6 +47,8 @@ from .workspace_pool import InferenceWorkspacePool
 __all__ = [
     "gelu_erf",
     "linear_bias_act",
+    "layernorm_affine_forward",
+    "layernorm_affine_add_residual_forward",
     "adaptive_layernorm_film_add_residual_forward",
     "adaptive_layernorm_film_forward",
     "unmerge_adaptive_layernorm_film_add_residual",

@@ -16,7 +16,7 @@ import torch
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libflash_aurora_b200.so")
 
-FA_F32, FA_BF16 = 0, 1
+FA_F32, FA_BF16, FA_F16 = 0, 1, 2
 FA_OK, FA_ERR_INVALID, FA_ERR_UNSUPPORTED, FA_ERR_CUDA, FA_ERR_TIMEOUT = 0, -1, -2, -3, -4
 FA_ATTN_BF16, FA_ATTN_FP32_3XTF32 = 0, 1
 FA_LAYOUT_BHND, FA_LAYOUT_BNC = 0, 1
@@ -62,6 +62,7 @@ SIGNATURES = {
                                              _u32, _vp]),
     "fa_window_attention_bias_noalloc": (_i32, [_i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64p, _vp,
                                                  _i64, _f32, _vp]),
+    "fa_layernorm_affine": (_i32, [_vp, _i32, _vp, _vp, _vp, _i32, _f32, _vp, _i64, _i64, _vp]),
     "fa_attention_status": (_i32, [ctypes.POINTER(ctypes.c_int)]),
     "fa_attention_status_reset": (_i32, [_vp]),
 }

@@ -19,8 +19,8 @@
 extern "C" {
 #endif
 
-/* Element types. */
-enum { FA_F32 = 0, FA_BF16 = 1 };
+/* Element types (FA_F16 only where a function says so). */
+enum { FA_F32 = 0, FA_BF16 = 1, FA_F16 = 2 };
 
 /* Status codes. */
 enum {
@@ -257,6 +257,17 @@ int fa_window_attention_bias_noalloc(int precision, int64_t Bwin, int64_t H, int
                                      const void* q, const void* k, const void* v, void* out,
                                      const int64_t strides[12], const float* bias, int64_t nW,
                                      float scale, void* stream);
+
+/*
+ * Perceiver decoder LayerNorm (+ residual): out = LayerNorm(x) * weight + bias (+ residual) over
+ * the last dimension D of `rows` contiguous rows, in fp32, rounded once to x's dtype. Replaces
+ * layernorm_affine_forward / layernorm_affine_add_residual_forward (ops/triton_perceiver_ln.py:25-47,
+ * kernel :101-145), called by aurora/model/perceiver.py:255-276. x_dtype: FA_F32, FA_BF16 or
+ * FA_F16; residual (nullable) and out have x's dtype and shape; weight / bias are (D,) of wb_dtype
+ * (any of the three). 1 <= D <= 4096. out may alias x or residual.
+ */
+int fa_layernorm_affine(const void* x, int x_dtype, const void* residual, const void* weight, const void* bias,
+                        int wb_dtype, float eps, void* out, int64_t rows, int64_t D, void* stream);
 
 /*
  * Device status word of the attention kernels: 0 when every bounded wait of every launch since

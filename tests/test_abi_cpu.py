@@ -131,3 +131,25 @@ def test_region_ids_fit_rule():
     assert region_ids_fit(np.tile(np.arange(16, dtype=np.uint8), (3, 9)))
     assert not region_ids_fit(np.tile(np.arange(17, dtype=np.uint8), (2, 1)))
     assert not region_ids_fit(np.full((2, 144), 40, dtype=np.uint8))
+
+
+def test_layernorm_arguments_return_status_without_a_gpu(lib):
+    from flash_aurora_b200 import _lib
+    p = ctypes.c_void_p(1 << 20)
+    rc = lib.fa_layernorm_affine(p, 3, None, p, p, 0, 1e-5, p, 4, 256, None)
+    assert rc == _lib.FA_ERR_INVALID and b"dtype" in lib.fa_last_error()
+    rc = lib.fa_layernorm_affine(p, 0, None, p, p, 0, 1e-5, p, 4, 4097, None)
+    assert rc == _lib.FA_ERR_UNSUPPORTED and b"4096" in lib.fa_last_error()
+    rc = lib.fa_layernorm_affine(None, 0, None, p, p, 0, 1e-5, p, 4, 256, None)
+    assert rc == _lib.FA_ERR_INVALID and b"null" in lib.fa_last_error()
+    assert lib.fa_layernorm_affine(None, 0, None, None, None, 0, 1e-5, None, 0, 256, None) == _lib.FA_OK
+
+
+def test_perceiver_ln_shim_rejects_like_upstream():
+    import torch
+    import flash_aurora_b200 as fa
+    x = torch.zeros(2, 3, 8)
+    with pytest.raises(ValueError, match="CUDA"):
+        fa.layernorm_affine_forward(x, torch.ones(8), torch.zeros(8), 1e-5)
+    with pytest.raises(ValueError, match="residual"):
+        fa.layernorm_affine_add_residual_forward(x, torch.zeros(2, 3, 9), torch.ones(8), torch.zeros(8), 1e-5)
