@@ -173,9 +173,9 @@ def _spawn(world, field_res, shift, mode):
     return out
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_gloo_ranks_match_field(world):
-    field_res = (4, 36, 72)
+@pytest.mark.parametrize("world,field_res", [(2, (4, 36, 72)), (4, (4, 36, 72)), (8, (4, 60, 24))])
+def test_gloo_ranks_match_field(world, field_res):
+    # world 8 over 10 window rows: bands of 1 or 2 window rows, uneven like config 5 at 8 GPUs
     out = _spawn(world, field_res, SHIFT, "ok")
     assert sorted(out) == list(range(world)), out
     for r, (kind, (ok_part, ok_trip)) in out.items():
