@@ -268,3 +268,29 @@ def test_fp32_tensor_memory_kernel_matches_warp_mma_kernel(monkeypatch, mask, N)
         assert _rel_l2(out, ref) <= 1e-5
         assert (out.cpu().double() - ref).abs().max().item() <= 2e-5
     assert (a - b).abs().max().item() <= 2e-5
+
+
+@pytest.mark.parametrize("N", [144, 120])
+def test_fp32_region_id_patterns_all_mask_modes(N):
+    """FP32 I/O with region ids of many shapes in one launch (one region, 2..8 regions, 9 or more,
+    ids >= 32, contiguous and scattered regions), against FP64 attention within the FP32-tier
+    bound."""
+    H, nW = 8, 8
+    g = torch.Generator().manual_seed(N)
+    ids = torch.zeros(nW, N, dtype=torch.uint8)
+    ids[0] = 4                                                              # one region
+    ids[1] = torch.where(torch.arange(N) < 50, 5, 9).to(torch.uint8)        # two regions
+    ids[2] = torch.randint(0, 8, (N,), generator=g).to(torch.uint8)         # up to 8 regions
+    ids[3] = (torch.arange(N) * 7 % 9).to(torch.uint8)                      # 9 regions: per logit
+    ids[4] = torch.randint(30, 36, (N,), generator=g).to(torch.uint8)       # ids >= 32: per logit
+    ids[5] = torch.where(torch.arange(N) % 3 == 0, 0, 31).to(torch.uint8)   # ids 0 and 31
+    ids[6] = torch.randint(0, 24, (N,), generator=g).to(torch.uint8)        # many regions: per logit
+    ids[7] = (torch.arange(N) // 18).to(torch.uint8)                        # 8 contiguous regions
+    bias = torch.where(ids[:, :, None] != ids[:, None, :], -100.0, 0.0)
+    Bwin = 3 * nW
+    q, k, v = _qkv(Bwin, H, N, 64, seed=21, scale=0.5)
+    a = fa.window_attn_fwd_cute(q.cuda(), k.cuda(), v.cuda(), precision=P.TF32_ACC_FP32, group_ids=ids.cuda())
+    ref = OB.window_attention_core(q.double(), k.double(), v.double(), bias.double())
+    for w in range(Bwin):
+        assert _rel_l2(a[w], ref[w]) <= 1e-5, w
+    assert (a.cpu().double() - ref).abs().max().item() <= 2e-5
