@@ -483,22 +483,6 @@ struct WindowRegions {
   int mode;
 };
 
-// Warp-cooperative: all 32 lanes must call it with the same window.
-__device__ __forceinline__ WindowRegions window_regions(const uint8_t* gi, int N, int lane) {
-  uint32_t pres = 0u, over = 0u;
-  for (int k = lane; k < N; k += 32) {
-    const uint32_t id = __ldg(gi + k);
-    if (id < 32u) pres |= 1u << id; else over = 1u;
-  }
-  pres = __reduce_or_sync(0xffffffffu, pres);
-  over = __reduce_or_sync(0xffffffffu, over);
-  const int distinct = __popc(pres);
-  WindowRegions r;
-  r.present = pres;
-  r.mode = over || distinct > 16 ? kModeBits : (distinct > 1 ? kModeUmma : kModeNone);
-  return r;
-}
-
 // Region-id masks (built into the mask UMMA) and masks with a per-logit path.
 template <int kMask> constexpr bool kRegions = kMask == kGroups || kMask == kGroupsFit;
 template <int kMask> constexpr bool kBitsPath = kMask == kGroups || kMask == kMaskU8;

@@ -98,21 +98,9 @@ ln_affine_kernel(const T* x, const T* res, const void* __restrict__ w, const voi
                  int64_t rows, int D, float eps) {
   // out may alias x or res: a warp reads its whole row before writing it. Up to D = 2048 the
   // residual row is requested together with x; weight and bias are re-read per row (L1 hits).
-  constexpr bool kKeepParams = false;
   constexpr bool kEarlyRes = kRes && kChunks <= 8;
   const int lane = threadIdx.x & 31;
   const float inv_d = 1.f / (float)D;
-  float wk[kKeepParams ? kChunks : 1][8], bk[kKeepParams ? kChunks : 1][8];
-  if constexpr (kKeepParams) {
-#pragma unroll
-    for (int i = 0; i < kChunks; ++i) {
-      const int col = (i * 32 + lane) * 8;
-      if (col < D) {
-        param8(w, wdt, col, wk[i]);
-        param8(b, wdt, col, bk[i]);
-      }
-    }
-  }
   for (int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows;
        row += (int64_t)gridDim.x * kWarpsPerBlock) {
     const T* xr = x + row * D;
@@ -149,17 +137,11 @@ ln_affine_kernel(const T* x, const T* res, const void* __restrict__ w, const voi
     for (int i = 0; i < kChunks; ++i) {
       const int col = (i * 32 + lane) * 8;
       if (col >= D) continue;
-      float y[8];
-      if constexpr (kKeepParams) {
+      float y[8], wv[8], bv[8];
+      param8(w, wdt, col, wv);
+      param8(b, wdt, col, bv);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) y[e] = (v[i][e] - mean) * rstd * wk[i][e] + bk[i][e];
-      } else {
-        float wv[8], bv[8];
-        param8(w, wdt, col, wv);
-        param8(b, wdt, col, bv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) y[e] = (v[i][e] - mean) * rstd * wv[e] + bv[e];
-      }
+      for (int e = 0; e < 8; ++e) y[e] = (v[i][e] - mean) * rstd * wv[e] + bv[e];
       if constexpr (kEarlyRes) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) y[e] += r[i][e];
