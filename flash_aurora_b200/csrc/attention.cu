@@ -1008,16 +1008,19 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       if (!mbar_wait(BAR(kXMax), (uint32_t)(i & 1), abort, p.status, 24, kTimeoutNs)) { ok = false; break; }
       const float m = fmaxf(pm, xmax[(g ^ 1) * 128 + row]);
       const float c = p.scale_log2, mc = -m * c;
+      // Paired fp32 FMAs and adds (two logits per instruction; each element's value is the same
+      // as with scalar fmaf).
+      const float2 c2 = make_float2(c, c), mc2 = make_float2(mc, mc);
       uint32_t pk[36];
-      float l8[4] = {0.f, 0.f, 0.f, 0.f};
+      float2 l2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int k = 0; k < 72; k += 2) {
-        const float a = ex2(fmaf(__uint_as_float(v[k]), c, mc));
-        const float b = ex2(fmaf(__uint_as_float(v[k + 1]), c, mc));
-        l8[(k >> 1) & 3] += a + b;
+        const float2 y = __ffma2_rn(make_float2(__uint_as_float(v[k]), __uint_as_float(v[k + 1])), c2, mc2);
+        const float a = ex2(y.x), b = ex2(y.y);
+        l2[(k >> 1) & 1] = __fadd2_rn(l2[(k >> 1) & 1], make_float2(a, b));
         pk[k >> 1] = pack_bf16x2(a, b);
       }
-      const float pl = (l8[0] + l8[1]) + (l8[2] + l8[3]);
+      const float pl = (l2[0].x + l2[0].y) + (l2[1].x + l2[1].y);
       // The row sum is only needed by the epilogue (1/l): publish this half's sum now and collect
       // the partner's after P is handed to the tensor cores, off the path to the PV UMMAs.
       xsum[g * 128 + row] = pl;
@@ -1192,19 +1195,21 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
       mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
       const float c = p.scale_log2, mca = -mxa * c, mcb = -mxb * c;
-      float la = 0.f, lb = 0.f;
+      const float2 c2 = make_float2(c, c), ma2 = make_float2(mca, mca), mb2 = make_float2(mcb, mcb);
+      float2 la2 = make_float2(0.f, 0.f), lb2 = make_float2(0.f, 0.f);
       uint32_t pa[18], pb[18];
 #pragma unroll
       for (int j = 0; j < 18; ++j) {
-        const float a0 = ex2(fmaf(__uint_as_float(v[4 * j]), c, mca));
-        const float a1 = ex2(fmaf(__uint_as_float(v[4 * j + 1]), c, mca));
-        const float b0 = ex2(fmaf(__uint_as_float(v[4 * j + 2]), c, mcb));
-        const float b1 = ex2(fmaf(__uint_as_float(v[4 * j + 3]), c, mcb));
-        la += a0 + a1;
-        lb += b0 + b1;
+        const float2 ya = __ffma2_rn(make_float2(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1])), c2, ma2);
+        const float2 yb =
+            __ffma2_rn(make_float2(__uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])), c2, mb2);
+        const float a0 = ex2(ya.x), a1 = ex2(ya.y), b0 = ex2(yb.x), b1 = ex2(yb.y);
+        la2 = __fadd2_rn(la2, make_float2(a0, a1));
+        lb2 = __fadd2_rn(lb2, make_float2(b0, b1));
         pa[j] = pack_bf16x2(a0, a1);
         pb[j] = pack_bf16x2(b0, b1);
       }
+      float la = la2.x + la2.y, lb = lb2.x + lb2.y;
       la += __shfl_xor_sync(0xffffffffu, la, 1);
       la += __shfl_xor_sync(0xffffffffu, la, 2);
       lb += __shfl_xor_sync(0xffffffffu, lb, 1);
