@@ -620,22 +620,26 @@ __device__ __forceinline__ void tmem_ld72(uint32_t taddr, uint32_t (&v)[72]) {
 template <bool kMasked, bool kFullN>
 __device__ __forceinline__ float raw_logits72(uint32_t (&v)[72], const uint32_t rel[3], float braw, int kbase,
                                               int N) {
-  float mx[8];
+  float mx[4];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) mx[e] = -INFINITY;
+  for (int e = 0; e < 4; ++e) mx[e] = -INFINITY;
 #pragma unroll
-  for (int k = 0; k < 72; ++k) {
-    float y = __uint_as_float(v[k]);
-    if constexpr (kMasked) {
-      if ((rel[k >> 5] >> (k & 31)) & 1u) y += braw;
+  for (int k = 0; k < 72; k += 2) {
+    float y[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      y[e] = __uint_as_float(v[k + e]);
+      if constexpr (kMasked) {
+        if ((rel[(k + e) >> 5] >> ((k + e) & 31)) & 1u) y[e] += braw;
+      }
+      if constexpr (!kFullN) {
+        if (kbase + k + e >= N) y[e] = -INFINITY;
+      }
+      v[k + e] = __float_as_uint(y[e]);
     }
-    if constexpr (!kFullN) {
-      if (kbase + k >= N) y = -INFINITY;
-    }
-    v[k] = __float_as_uint(y);
-    mx[k & 7] = fmaxf(mx[k & 7], y);
+    mx[(k >> 1) & 3] = fmax3(mx[(k >> 1) & 3], y[0], y[1]);
   }
-  return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+  return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
 }
 
 template <int kMask, bool kFullN>
@@ -943,11 +947,14 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       // writes the whole tile with one bulk tensor store (rows past N are dropped by it).
       (void)t;
       const float inv = 1.f / l;
+      const float2 inv2 = make_float2(inv, inv);
       uint32_t pk[16];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        pk[e] = pack_bf16x2(__uint_as_float(o0[2 * e]) * inv, __uint_as_float(o0[2 * e + 1]) * inv);
-        pk[8 + e] = pack_bf16x2(__uint_as_float(o1[2 * e]) * inv, __uint_as_float(o1[2 * e + 1]) * inv);
+        const float2 y0 = __fmul2_rn(make_float2(__uint_as_float(o0[2 * e]), __uint_as_float(o0[2 * e + 1])), inv2);
+        const float2 y1 = __fmul2_rn(make_float2(__uint_as_float(o1[2 * e]), __uint_as_float(o1[2 * e + 1])), inv2);
+        pk[e] = pack_bf16x2(y0.x, y0.y);
+        pk[8 + e] = pack_bf16x2(y1.x, y1.y);
       }
       const uint32_t stg = sbase + (j % kStages) * kStageBytes + (uint32_t)kQKBytes + (uint32_t)row * 128u;
 #pragma unroll
@@ -1073,13 +1080,16 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       // Rows 128..143 of the tile's staged output (see the softmax epilogue).
       (void)t;
       const float ia = 1.f / la, ib = 1.f / lb;
+      const float2 ia2 = make_float2(ia, ia), ib2 = make_float2(ib, ib);
       const uint32_t stg = sbase + (j % kStages) * kStageBytes + (uint32_t)kQKBytes;
 #pragma unroll
       for (int jd = 0; jd < 8; ++jd) {
+        const float2 ya = __fmul2_rn(make_float2(__uint_as_float(o[4 * jd]), __uint_as_float(o[4 * jd + 1])), ia2);
+        const float2 yb = __fmul2_rn(make_float2(__uint_as_float(o[4 * jd + 2]), __uint_as_float(o[4 * jd + 3])), ib2);
         st_shared_u32(stg + (uint32_t)ra * 128u + (uint32_t)(((jd ^ (ra & 7)) & 7) << 4) + 4u * t0,
-                      pack_bf16x2(__uint_as_float(o[4 * jd]) * ia, __uint_as_float(o[4 * jd + 1]) * ia));
+                      pack_bf16x2(ya.x, ya.y));
         st_shared_u32(stg + (uint32_t)rb * 128u + (uint32_t)(((jd ^ (rb & 7)) & 7) << 4) + 4u * t0,
-                      pack_bf16x2(__uint_as_float(o[4 * jd + 2]) * ib, __uint_as_float(o[4 * jd + 3]) * ib));
+                      pack_bf16x2(yb.x, yb.y));
       }
       fence_proxy_async_shared();
       __syncwarp();
@@ -1168,9 +1178,9 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
             }
             v[4 * j + e] = __float_as_uint(ya);
             v[4 * j + 2 + e] = __float_as_uint(yb);
-            mxa = fmaxf(mxa, ya);
-            mxb = fmaxf(mxb, yb);
           }
+          mxa = fmax3(mxa, __uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]));
+          mxb = fmax3(mxb, __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
         }
       } else {
 #pragma unroll
@@ -1185,9 +1195,9 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
             }
             v[4 * j + e] = __float_as_uint(ya);
             v[4 * j + 2 + e] = __float_as_uint(yb);
-            mxa = fmaxf(mxa, ya);
-            mxb = fmaxf(mxb, yb);
           }
+          mxa = fmax3(mxa, __uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]));
+          mxb = fmax3(mxb, __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
         }
       }
       mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));

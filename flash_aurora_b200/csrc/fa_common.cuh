@@ -182,6 +182,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// Three-input fp32 maximum (one instruction on sm_100; PTX ISA 8.8). NaN handling is that of
+// fmaxf: a NaN operand is ignored unless all are NaN.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   // bf16 -> fp32 is exact: the bf16 bits are the top half of the fp32 pattern.
   return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
