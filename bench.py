@@ -447,7 +447,8 @@ def run_attention(args) -> None:
 
 
 def run_layout_adaln(args) -> None:
-    """Config 3: grid (4,45,90), D 2048, padded (4,48,96) -> 128 windows, shift (1,3,6)."""
+    """Config 3 layout and AdaLN kernels (grid (4,45,90), D 2048, padded (4,48,96) -> 128 windows,
+    shift (1,3,6)), then the config-4 per-stage AdaLN, GELU, Perceiver LN and fc1 + GELU launches."""
     import flash_aurora_b200 as fa
     dev = torch.device("cuda", 0)
     hbm, _, kind = _peaks()
@@ -502,9 +503,38 @@ def run_layout_adaln(args) -> None:
                           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                                        "frac": round(gbs / hbm, 3), "peak_kind": kind, "algorithmic_bytes": nbytes}}),
               flush=True)
+    del h, lat, lat_res, x, win, branch, resid
+    # AdaLN as the config-4 backbone launches it at each stage: norm1 fused with the window unmerge
+    # (bf16 windows in, fp32 residual and output, bf16 copy out) and norm2 fused with the next
+    # block's partition (bf16 x, fp32 residual and output, bf16 windows out): 12 bytes per element.
+    from flash_aurora_b200.adaln import adaptive_layernorm_film_add_residual_partition
+    for tag, sres, sD in (("S1", (4, 180, 360), 512), ("S2", (4, 90, 180), 1024), ("S3", (4, 45, 90), 2048)):
+        sL = sres[0] * sres[1] * sres[2]
+        xs = torch.randn(1, *sres, sD, device=dev, generator=g)
+        wins = fa.roll_pad_partition_windows(xs, sres, ws, ss, out_dtype=torch.bfloat16)
+        del xs
+        rs = torch.randn(1, sL, sD, device=dev, generator=g)
+        hs = torch.randn(1, sL, sD, device=dev, generator=g).bfloat16()
+        scs = torch.randn(1, 1, sD, device=dev, generator=g) * 0.1
+        shs = torch.randn(1, 1, sD, device=dev, generator=g) * 0.1
+        x1b = torch.empty(1, sL, sD, device=dev, dtype=torch.bfloat16)
+        nxt = torch.zeros_like(wins)
+        for name, fn in (
+                ("norm1 unmerge + AdaLN + residual (+ bf16 copy)",
+                 lambda: fa.unmerge_adaptive_layernorm_film_add_residual(wins, rs, scs, shs, sres, ws, ss, 0.0, 1e-5,
+                                                                         out_bf16=x1b)),
+                ("norm2 AdaLN + residual + next partition",
+                 lambda: adaptive_layernorm_film_add_residual_partition(rs, hs, scs, shs, sres, ws, ss, nxt))):
+            ms = _time_launches(fn, args.steps, flush=flush)
+            nbytes = sL * sD * 12
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            print(json.dumps({"workload": f"config4 {tag} {name} (L={sL}, D={sD})", "ms": round(ms, 4),
+                              "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                           "frac": round(gbs / hbm, 3), "peak_kind": kind,
+                                           "algorithmic_bytes": nbytes}}), flush=True)
+        del wins, rs, hs, x1b, nxt
     # The block MLP's fc1 + GELU at each stage of config 4: fused tensor-core kernel vs cuBLAS + GELU.
     _, tf_peak, _ = _peaks()
-    del h, lat, lat_res
     for tag, M, K, N in (("S1", 259200, 512, 2048), ("S2", 64800, 1024, 4096), ("S3", 16200, 2048, 8192)):
         a = torch.randn(M, K, device=dev, generator=g).bfloat16()
         w = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()

@@ -59,8 +59,9 @@ struct AdaArgs {
 };
 
 // kChunks = number of 8-element (vector path) or 1-element (scalar path) chunks per lane.
+// Rows of up to 512 elements fit in 64 registers per thread, four 256-thread blocks per SM.
 template <typename TX, typename TO, bool kVec, int kChunks>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) adaln_kernel(AdaArgs a) {
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, (kVec && kChunks <= 2) ? 4 : 2) adaln_kernel(AdaArgs a) {
   constexpr int kE = kVec ? 8 : 1;  // elements per chunk per lane
   const int lane = threadIdx.x & 31;
   const int D = a.D;
@@ -70,24 +71,30 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) adaln_kernel(AdaArgs a) {
   TO* __restrict__ og = reinterpret_cast<TO*>(a.out);
   const float inv_d = 1.0f / (float)D;
 
-  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows;
-       row += (int64_t)gridDim.x * kWarpsPerBlock) {
+  // Address of the LN input row of token row `r` (window gather in the unmerge form).
+  auto x_row = [&](int64_t r) -> const TX* {
+    if (!a.gather) return xwin + r * D;
+    const int64_t b = r / a.L;
+    const int32_t t = (int32_t)(r - b * a.L);
+    const int32_t w = t % a.lp.W;
+    const int32_t h = (t / a.lp.W) % a.lp.Hout;
+    const int32_t c = t / (a.lp.W * a.lp.Hout);
+    const int32_t slot = unmerge_slot(a.lp, c, h, w);
+    if (slot >= 0) return xwin + (b * (int64_t)a.lp.nW * a.lp.N + slot) * D;
+    // Band mode: row computed by the previous band, received into the halo-back buffer.
+    return reinterpret_cast<const TX*>(a.halo_in) + (b * (int64_t)a.lp.C * a.lp.band * a.lp.W + (-1 - slot)) * D;
+  };
+  const int64_t stride = (int64_t)gridDim.x * kWarpsPerBlock;
+  const int64_t first = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (kVec && lane == 0 && rg && first < rows) prefetch_l2_bulk(rg + first * D, (uint32_t)(D * sizeof(TO)));
+  for (int64_t row = first; row < rows; row += stride) {
     const int64_t b = row / a.L;
-    int64_t xrow = row;
-    const TX* xg = xwin;
-    if (a.gather) {
-      const int32_t t = (int32_t)(row - b * a.L);
-      const int32_t w = t % a.lp.W;
-      const int32_t h = (t / a.lp.W) % a.lp.Hout;
-      const int32_t c = t / (a.lp.W * a.lp.Hout);
-      const int32_t slot = unmerge_slot(a.lp, c, h, w);
-      if (slot >= 0) {
-        xrow = b * (int64_t)a.lp.nW * a.lp.N + slot;
-      } else {
-        // Band mode: row computed by the previous band, received into the halo-back buffer.
-        xg = reinterpret_cast<const TX*>(a.halo_in);
-        xrow = b * (int64_t)a.lp.C * a.lp.band * a.lp.W + (-1 - slot);
-      }
+    const TX* xr = x_row(row);
+    if (kVec && lane == 0 && row + stride < rows) {
+      // The next row's input and residual stream into L2 while this row is reduced, so that the
+      // per-warp chain (load, two reductions, residual load, store) waits less on DRAM.
+      prefetch_l2_bulk(x_row(row + stride), (uint32_t)(D * sizeof(TX)));
+      if (rg) prefetch_l2_bulk(rg + (row + stride) * D, (uint32_t)(D * sizeof(TO)));
     }
     int64_t wrow = -1;
     if (a.win_out) {
@@ -97,7 +104,6 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) adaln_kernel(AdaArgs a) {
       const int32_t c = t / (a.wlp.W * a.wlp.H);
       wrow = b * (int64_t)a.wlp.nW * a.wlp.N + unmerge_slot(a.wlp, c, h, w);
     }
-    const TX* xr = xg + xrow * D;
     float v[kChunks][kE];
     float s = 0.f;
 #pragma unroll

@@ -182,6 +182,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// Bulk prefetch of `bytes` (a multiple of 16) from a 16-byte-aligned global address into L2. A
+// hint: nothing waits for it and it writes no register or shared memory.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Three-input fp32 maximum (one instruction on sm_100; PTX ISA 8.8). NaN handling is that of
 // fmaxf: a NaN operand is ignored unless all are NaN.
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
