@@ -5,6 +5,8 @@
 // 16-byte vector accesses. The index arithmetic is done once per row, not per element as in
 // the upstream Triton kernels (ops/triton_swin3d_layout.py:192-307). Reads of the source use
 // the non-allocating streaming path: each source row is read exactly once.
+#include <type_traits>
+
 #include "fa_common.cuh"
 
 namespace fa {
@@ -12,8 +14,16 @@ namespace {
 
 constexpr int kWarpsPerBlock = 8;
 
+// Blocks per SM the register budget must allow. fp32 -> fp32 rows move two 8-float vectors per
+// lane and step; at the 40 registers ptxas picks for them unbounded they spill, so they get 64
+// (four blocks). The other type pairs fit in 40 registers (six blocks).
+template <typename TIn, typename TOut>
+constexpr int min_blocks() {
+  return (std::is_same<TIn, float>::value && std::is_same<TOut, float>::value) ? 4 : 6;
+}
+
 template <typename TIn, typename TOut, bool kVec>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, min_blocks<TIn, TOut>())
 partition_kernel(const TIn* __restrict__ x, const TIn* __restrict__ halo, TOut* __restrict__ out,
                  LayoutParams p, int64_t B, int32_t D) {
   const int lane = threadIdx.x & 31;
@@ -52,7 +62,7 @@ partition_kernel(const TIn* __restrict__ x, const TIn* __restrict__ halo, TOut* 
 }
 
 template <typename TIn, typename TOut, bool kVec>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, min_blocks<TIn, TOut>())
 unmerge_kernel(const TIn* __restrict__ win, const TIn* __restrict__ halo_in, TOut* __restrict__ out,
                LayoutParams p, int64_t B, int32_t D) {
   const int lane = threadIdx.x & 31;
