@@ -47,7 +47,7 @@ UNIT = "ms/step"
 CONFIG4 = dict(embed_dim=512, encoder_depths=(6, 10, 8), encoder_num_heads=(8, 16, 32),
                decoder_depths=(8, 10, 6), decoder_num_heads=(32, 16, 8), window_size=(2, 6, 12))
 PATCH_RES = (4, 180, 360)
-TRAFFIC_RATIO = 0.976  # attention DRAM bytes / algorithmic bytes, ncu (profiles/attention_config2_tcgen05.md)
+TRAFFIC_RATIO = 0.973  # attention DRAM bytes / algorithmic bytes, ncu (profiles/attention_config2_tcgen05.md)
 STAGES = [((4, 180, 360), 512, 8, 12), ((4, 90, 180), 1024, 16, 20), ((4, 45, 90), 2048, 32, 16)]
 
 
@@ -270,7 +270,7 @@ def run_b200(args) -> None:
     hbm, _, peak_kind = _peaks()
     achieved = attn_bytes / (attn_ms * 1e-3) / 1e9 if attn_ms > 0 else 0.0
     # DRAM traffic per launch: the ncu capture of config-2 launches measured
-    # dram__bytes_read + dram__bytes_write = 0.973-0.979 x the algorithmic bytes (Q, K, V once,
+    # dram__bytes_read + dram__bytes_write = 0.973 x the algorithmic bytes (Q, K, V once,
     # part of O still in L2 at exit); the same ratio is applied to this step's average launch.
     traffic = round(TRAFFIC_RATIO * attn_bytes / attn_launches) if attn_launches else None
     # Per block: attention, unmerge+AdaLN1, GELU, AdaLN2 (fused with the next block's partition);
@@ -292,7 +292,7 @@ def run_b200(args) -> None:
         "roofline": {"kernel": "window attention (bf16, per-launch average over an eager pass of the same steps)",
                      "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 3), "traffic": traffic,
-                     "traffic_source": "ncu config-2 capture ratio 0.976 x this step's bytes per launch",
+                     "traffic_source": "ncu config-2 capture ratio 0.973 x this step's bytes per launch",
                      "algorithmic_bytes_per_launch": round(attn_bytes / attn_launches) if attn_launches else None,
                      "peak_kind": peak_kind,
                      "tflops": round(attn_flops / (attn_ms * 1e-3) / 1e12, 1) if attn_ms > 0 else None,
