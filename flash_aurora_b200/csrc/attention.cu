@@ -1310,6 +1310,10 @@ constexpr int kVtSw32 = 4 * 64 * 128;
 constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // {max, sum} x warpgroup x row
 constexpr int kThreads = 512;
 constexpr int kConvThreads = 128;             // warps 12..15
+// Registers per thread after the per-warpgroup split (launched at 128 for 512 threads).
+constexpr uint32_t kRegsLaunch = 128, kRegsSoftmax = 136, kRegsConvert = 112;
+static_assert(4 * 32 * kRegsLaunch + 8 * 32 * kRegsSoftmax + 4 * 32 * kRegsConvert == kThreads * kRegsLaunch,
+              "register split must add up to the launch budget");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 160, kColSR = 224, kColOR = 384;
 constexpr uint32_t kLaneHalf = 16u << 16;  // second lane half of an M=64 block
@@ -1427,6 +1431,10 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
     }
   } else if (warp >= 12) {
     // ---------------- hi / lo split of each landed tile ----------------
+    // Register split (512 threads launched at 128): warpgroup 0 (TMA, issuer, rows 128..143) keeps
+    // 128, the two softmax warpgroups take 136, this one gives up 16:
+    // 128*128 + 256*136 + 128*112 = 65536 = 512*128.
+    warpgroup_reg_dealloc<kRegsConvert>();
     const int ct = threadIdx.x - 12 * 32;
     for (int i = 0; i < n_local; ++i) {
       const uint32_t par = (uint32_t)(i & 1);
@@ -1546,6 +1554,7 @@ attn_tc_tf32_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
     }
   } else if (warp >= 4) {
     // ---------------- rows 0..127: softmax, P, output rows ----------------
+    warpgroup_reg_alloc<kRegsSoftmax>();
     const int g = (warp - 4) >> 2;  // key columns 72g .. 72g+71, output columns 32g .. 32g+31
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;

@@ -87,6 +87,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 // ------------------------------------------------------------------------------------------
 // TMA (bulk tensor copies, global -> shared::cta, completion on an mbarrier)
 // ------------------------------------------------------------------------------------------
+// Per-warpgroup register budget changes (all four warps of a warpgroup execute the same one). The
+// budgets of all warpgroups must add up to the registers the block was launched with, or an
+// increase waits for registers that are never released.
+template <uint32_t kRegs>
+__device__ __forceinline__ void warpgroup_reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void warpgroup_reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
