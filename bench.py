@@ -446,6 +446,44 @@ def run_attention(args) -> None:
             }), flush=True)
 
 
+def run_adaln_stages(args, flush=None) -> None:
+    """AdaLN as the config-4 backbone launches it at each stage: norm1 fused with the window unmerge
+    (bf16 windows in, fp32 residual and output, bf16 copy out) and norm2 fused with the next block's
+    partition (bf16 x, fp32 residual and output, bf16 windows out): 12 bytes per element."""
+    import flash_aurora_b200 as fa
+    from flash_aurora_b200.adaln import adaptive_layernorm_film_add_residual_partition
+    dev = torch.device("cuda", 0)
+    hbm, _, kind = _peaks()
+    flush = flush or L2Flush(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    ws, ss = (2, 6, 12), (1, 3, 6)
+    for tag, sres, sD in (("S1", (4, 180, 360), 512), ("S2", (4, 90, 180), 1024), ("S3", (4, 45, 90), 2048)):
+        sL = sres[0] * sres[1] * sres[2]
+        xs = torch.randn(1, *sres, sD, device=dev, generator=g)
+        wins = fa.roll_pad_partition_windows(xs, sres, ws, ss, out_dtype=torch.bfloat16)
+        del xs
+        rs = torch.randn(1, sL, sD, device=dev, generator=g)
+        hs = torch.randn(1, sL, sD, device=dev, generator=g).bfloat16()
+        scs = torch.randn(1, 1, sD, device=dev, generator=g) * 0.1
+        shs = torch.randn(1, 1, sD, device=dev, generator=g) * 0.1
+        x1b = torch.empty(1, sL, sD, device=dev, dtype=torch.bfloat16)
+        nxt = torch.zeros_like(wins)
+        for name, fn in (
+                ("norm1 unmerge + AdaLN + residual (+ bf16 copy)",
+                 lambda: fa.unmerge_adaptive_layernorm_film_add_residual(wins, rs, scs, shs, sres, ws, ss, 0.0, 1e-5,
+                                                                         out_bf16=x1b)),
+                ("norm2 AdaLN + residual + next partition",
+                 lambda: adaptive_layernorm_film_add_residual_partition(rs, hs, scs, shs, sres, ws, ss, nxt))):
+            ms = _time_launches(fn, args.steps, flush=flush)
+            nbytes = sL * sD * 12
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            print(json.dumps({"workload": f"config4 {tag} {name} (L={sL}, D={sD})", "ms": round(ms, 4),
+                              "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                           "frac": round(gbs / hbm, 3), "peak_kind": kind,
+                                           "algorithmic_bytes": nbytes}}), flush=True)
+        del wins, rs, hs, x1b, nxt
+
+
 def run_layout_adaln(args) -> None:
     """Config 3 layout and AdaLN kernels (grid (4,45,90), D 2048, padded (4,48,96) -> 128 windows,
     shift (1,3,6)), then the config-4 per-stage AdaLN, GELU, Perceiver LN and fc1 + GELU launches."""
@@ -504,35 +542,7 @@ def run_layout_adaln(args) -> None:
                                        "frac": round(gbs / hbm, 3), "peak_kind": kind, "algorithmic_bytes": nbytes}}),
               flush=True)
     del h, lat, lat_res, x, win, branch, resid
-    # AdaLN as the config-4 backbone launches it at each stage: norm1 fused with the window unmerge
-    # (bf16 windows in, fp32 residual and output, bf16 copy out) and norm2 fused with the next
-    # block's partition (bf16 x, fp32 residual and output, bf16 windows out): 12 bytes per element.
-    from flash_aurora_b200.adaln import adaptive_layernorm_film_add_residual_partition
-    for tag, sres, sD in (("S1", (4, 180, 360), 512), ("S2", (4, 90, 180), 1024), ("S3", (4, 45, 90), 2048)):
-        sL = sres[0] * sres[1] * sres[2]
-        xs = torch.randn(1, *sres, sD, device=dev, generator=g)
-        wins = fa.roll_pad_partition_windows(xs, sres, ws, ss, out_dtype=torch.bfloat16)
-        del xs
-        rs = torch.randn(1, sL, sD, device=dev, generator=g)
-        hs = torch.randn(1, sL, sD, device=dev, generator=g).bfloat16()
-        scs = torch.randn(1, 1, sD, device=dev, generator=g) * 0.1
-        shs = torch.randn(1, 1, sD, device=dev, generator=g) * 0.1
-        x1b = torch.empty(1, sL, sD, device=dev, dtype=torch.bfloat16)
-        nxt = torch.zeros_like(wins)
-        for name, fn in (
-                ("norm1 unmerge + AdaLN + residual (+ bf16 copy)",
-                 lambda: fa.unmerge_adaptive_layernorm_film_add_residual(wins, rs, scs, shs, sres, ws, ss, 0.0, 1e-5,
-                                                                         out_bf16=x1b)),
-                ("norm2 AdaLN + residual + next partition",
-                 lambda: adaptive_layernorm_film_add_residual_partition(rs, hs, scs, shs, sres, ws, ss, nxt))):
-            ms = _time_launches(fn, args.steps, flush=flush)
-            nbytes = sL * sD * 12
-            gbs = nbytes / (ms * 1e-3) / 1e9
-            print(json.dumps({"workload": f"config4 {tag} {name} (L={sL}, D={sD})", "ms": round(ms, 4),
-                              "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
-                                           "frac": round(gbs / hbm, 3), "peak_kind": kind,
-                                           "algorithmic_bytes": nbytes}}), flush=True)
-        del wins, rs, hs, x1b, nxt
+    run_adaln_stages(args, flush)
     # The block MLP's fc1 + GELU at each stage of config 4: fused tensor-core kernel vs cuBLAS + GELU.
     _, tf_peak, _ = _peaks()
     for tag, M, K, N in (("S1", 259200, 512, 2048), ("S2", 64800, 1024, 4096), ("S3", 16200, 2048, 8192)):
@@ -559,7 +569,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sharded", action="store_true", help="skip the config-5 sharded-stage object")
-    ap.add_argument("--workload", choices=["backbone", "attention", "layout_adaln", "sharded"], default="backbone")
+    ap.add_argument("--workload", choices=["backbone", "attention", "layout_adaln", "adaln_stages", "sharded"], default="backbone")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -567,6 +577,8 @@ def main() -> None:
         return run_attention(args)
     if args.workload == "layout_adaln":
         return run_layout_adaln(args)
+    if args.workload == "adaln_stages":
+        return run_adaln_stages(args)
     if args.workload == "sharded" and args.impl != "reference":
         return run_sharded(args)
     if args.impl == "reference":

@@ -66,9 +66,9 @@ def test_output_dtypes_follow_upstream():
 @pytest.mark.parametrize("res,ws,ss", [((4, 36, 72), (2, 6, 12), (1, 3, 6)), ((4, 45, 90), (2, 6, 12), (1, 3, 6)),
                                        ((3, 13, 25), (2, 6, 12), (0, 0, 0))])
 @pytest.mark.parametrize("wdt", [torch.float32, torch.bfloat16])
-def test_unmerge_fused_equals_composition(res, ws, ss, wdt):
+@pytest.mark.parametrize("D", [256, 1024])
+def test_unmerge_fused_equals_composition(res, ws, ss, wdt, D):
     g = torch.Generator().manual_seed(1)
-    D = 256
     gm = OL.geometry(res, ws, ss)
     B = 2
     L = res[0] * res[1] * res[2]
