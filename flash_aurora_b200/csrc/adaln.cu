@@ -59,7 +59,8 @@ struct AdaArgs {
 };
 
 // kChunks = number of 8-element (vector path) or 1-element (scalar path) chunks per lane.
-// Rows of up to 512 elements fit in 64 registers per thread, four 256-thread blocks per SM.
+// Register bound: vector rows of up to 512 elements are held to 64 registers per thread (four
+// 256-thread blocks per SM), everything else to 128 (two blocks).
 template <typename TX, typename TO, bool kVec, int kChunks>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32, (kVec && kChunks <= 2) ? 4 : 2) adaln_kernel(AdaArgs a) {
   constexpr int kE = kVec ? 8 : 1;  // elements per chunk per lane
