@@ -249,6 +249,7 @@ def run_b200(args) -> None:
         torch.cuda.synchronize()
         WA.set_recorder(None)
         attn_ms, attn_bytes, attn_flops, attn_launches = rec.totals()
+        attn_shapes = rec.by_shape()
 
         # End to end from pinned host memory through the public API: every step uploads its
         # input and downloads its full output; HostPipeline overlaps those copies with the
@@ -296,7 +297,10 @@ def run_b200(args) -> None:
                      "algorithmic_bytes_per_launch": round(attn_bytes / attn_launches) if attn_launches else None,
                      "peak_kind": peak_kind,
                      "tflops": round(attn_flops / (attn_ms * 1e-3) / 1e12, 1) if attn_ms > 0 else None,
-                     "launches": attn_launches, "kernel_ms_per_step": round(attn_ms / args.steps, 3)},
+                     "launches": attn_launches, "kernel_ms_per_step": round(attn_ms / args.steps, 3),
+                     # per launch size (one per backbone stage): fraction of the peak each stage reaches
+                     "by_launch_size": [{"bytes": nb, "launches": n, "ms": round(t, 4),
+                                         "frac": round(nb / (t * 1e-3) / 1e9 / hbm, 3)} for nb, n, t in attn_shapes]},
         "clocks": clocks,
     }
     del model, x, y, yy, graphed, pipe

@@ -52,6 +52,14 @@ class KernelRecorder:
         ms = sum(a.elapsed_time(b) for a, b, _, _ in self.records)
         return ms, sum(r[2] for r in self.records), sum(r[3] for r in self.records), len(self.records)
 
+    def by_shape(self) -> list[tuple[int, int, float]]:
+        """(bytes per launch, launches, average milliseconds) per distinct launch size, largest
+        first: the per-stage view of the same launches."""
+        acc: dict[int, list[float]] = {}
+        for a, b, nbytes, _ in self.records:
+            acc.setdefault(nbytes, []).append(a.elapsed_time(b))
+        return [(nb, len(v), sum(v) / len(v)) for nb, v in sorted(acc.items(), key=lambda kv: -kv[0])]
+
 
 _RECORDER: Optional[KernelRecorder] = None
 
