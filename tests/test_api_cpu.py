@@ -91,3 +91,23 @@ def test_lead_time_expansion_matches_oracle():
     from oracle.block import lead_time_expansion as ref
     h = torch.tensor([6.0, 0.5])
     torch.testing.assert_close(lead_time_expansion(h, 512), ref(h, 512), rtol=0, atol=0)
+
+
+def test_kernel_recorder_groups_launches_by_size():
+    """The per-stage view the backbone bench line reports: launches grouped by their algorithmic
+    bytes, largest first, with the average time of each group (events faked on the host)."""
+    from flash_aurora_b200.window_attn import KernelRecorder
+
+    class Ev:
+        def __init__(self, t):
+            self.t = t
+
+        def elapsed_time(self, other):
+            return other.t - self.t
+
+    rec = KernelRecorder()
+    for nbytes, ms in ((300, 1.0), (900, 3.0), (300, 3.0), (600, 2.0), (900, 5.0)):
+        rec.records.append((Ev(0.0), Ev(ms), nbytes, 4 * nbytes))
+    assert rec.by_shape() == [(900, 2, 4.0), (600, 1, 2.0), (300, 2, 2.0)]
+    total_ms, total_bytes, total_flops, launches = rec.totals()
+    assert (total_ms, total_bytes, total_flops, launches) == (14.0, 3300, 13200, 5)
