@@ -111,3 +111,18 @@ def test_kernel_recorder_groups_launches_by_size():
     assert rec.by_shape() == [(900, 2, 4.0), (600, 1, 2.0), (300, 2, 2.0)]
     total_ms, total_bytes, total_flops, launches = rec.totals()
     assert (total_ms, total_bytes, total_flops, launches) == (14.0, 3000, 12000, 5)
+
+
+def test_maybe_adjust_windows_matches_oracle():
+    """The package's window clamp equals the oracle's restatement of upstream util.py:54-72 (which
+    the layout fixtures pin), including the assertion on a zero-sized axis."""
+    import itertools
+
+    from flash_aurora_b200.util import maybe_adjust_windows
+    from oracle import layout as OL
+
+    for res, ws, ss in itertools.product([(4, 45, 90), (2, 6, 12), (1, 5, 7), (3, 13, 25)],
+                                         [(2, 6, 12), (4, 6, 12), (1, 1, 1)], [(0, 0, 0), (1, 3, 6)]):
+        assert maybe_adjust_windows(ws, ss, res) == OL.maybe_adjust_windows(ws, ss, res)
+    with pytest.raises(AssertionError, match="Window size must be positive"):
+        maybe_adjust_windows((2, 6, 12), (1, 3, 6), (0, 6, 12))
