@@ -1,0 +1,76 @@
+"""Register budgets of the memory-bound kernels, checked at compile time (no GPU).
+
+The row kernels are tuned with `__launch_bounds__` so that their vector paths keep every value in
+registers. Unbounded, ptxas chose 40 registers for the fp32 -> fp32 layout copies and spilled
+24-36 bytes, which cost them 6-8 % of their bandwidth. These tests compile the sources for sm_100a
+with `-Xptxas -v` and fail if a vector-path instantiation spills again.
+"""
+
+from __future__ import annotations
+
+import os
+import re
+import shutil
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+CSRC = os.path.join(ROOT, "flash_aurora_b200", "csrc")
+NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+
+pytestmark = pytest.mark.skipif(not os.path.exists(NVCC), reason="nvcc not available")
+
+
+def _ptxas_report(source: str, tmp_path) -> dict[str, tuple[int, int]]:
+    """{mangled kernel name: (registers, spill-store bytes)} for every entry of `source`."""
+    out = subprocess.run(
+        [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-Xptxas", "-v",
+         "-I" + os.path.join(ROOT, "include"), "-I" + CSRC, "-c", os.path.join(CSRC, source),
+         "-o", str(tmp_path / "k.o")],
+        capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    report: dict[str, tuple[int, int]] = {}
+    name, spill = None, 0
+    for line in out.stderr.splitlines():
+        m = re.search(r"Compiling entry function '(\S+)'", line)
+        if m:
+            name, spill = m.group(1), 0
+            continue
+        m = re.search(r"(\d+) bytes spill stores", line)
+        if m and name:
+            spill = int(m.group(1))
+        m = re.search(r"Used (\d+) registers", line)
+        if m and name:
+            report[name] = (int(m.group(1)), spill)
+            name = None
+    return report
+
+
+def test_layout_kernels_do_not_spill(tmp_path):
+    report = _ptxas_report("layout.cu", tmp_path)
+    kernels = {k: v for k, v in report.items() if "partition_kernel" in k or "unmerge_kernel" in k}
+    assert len(kernels) >= 12, sorted(kernels)
+    spilled = {k: v for k, v in kernels.items() if v[1] > 0}
+    assert not spilled, spilled
+
+
+def test_adaln_vector_kernels_do_not_spill(tmp_path):
+    report = _ptxas_report("adaln.cu", tmp_path)
+    # Vector-path instantiations carry `Lb1E` (kVec = true) in their mangled names.
+    vec = {k: v for k, v in report.items() if "adaln_kernel" in k and "Lb1E" in k}
+    assert len(vec) >= 8, sorted(vec)
+    spilled = {k: v for k, v in vec.items() if v[1] > 0}
+    assert not spilled, spilled
+    # D <= 512 rows are held to 64 registers (four 256-thread blocks per SM).
+    small = {k: v for k, v in vec.items() if re.search(r"Lb1ELi[12]E", k)}
+    assert small and all(r <= 64 for r, _ in small.values()), small
+
+
+def test_fused_gemm_does_not_spill(tmp_path):
+    report = _ptxas_report("gemm.cu", tmp_path)
+    kernels = {k: v for k, v in report.items() if "gemm_bias_act_kernel" in k}
+    assert len(kernels) == 2, sorted(kernels)
+    spilled = {k: v for k, v in kernels.items() if v[1] > 0}
+    assert not spilled, spilled
