@@ -13,6 +13,8 @@ PyTorch host layer that mirrors the operator interface of upstream Flash-Aurora:
 * ``swin3d``         Swin3DTransformerBlock / Swin3DTransformerBackbone with upstream state-dict
                      keys (upstream ``aurora/model/swin3d.py``, ``film.py``)
 * ``sharding``       latitude-band window sharding with a point-to-point halo exchange
+* ``custom_op_paths`` can_use_* gating predicates (upstream ``aurora/model/custom_op_paths.py``)
+* ``status``         device-side failure status of the pipelined kernels, checked on the host
 """
 
 from .activation import gelu_erf
@@ -43,6 +45,14 @@ from .window_attn import (
     window_attn_fwd_cute_qkvpacked,
 )
 from .workspace_pool import InferenceWorkspacePool
+from .status import DeviceStatusError, check_device_status, device_status, reset_device_status, watchdog_selftest
+from .custom_op_paths import (
+    can_use_cute_qkvpacked,
+    can_use_cute_window_attention,
+    can_use_triton_adaln,
+    can_use_triton_gelu,
+    can_use_triton_layout,
+)
 
 __all__ = [
     "gelu_erf",
@@ -72,4 +82,14 @@ __all__ = [
     "window_attn_fwd_cute",
     "window_attn_fwd_cute_qkvpacked",
     "InferenceWorkspacePool",
+    "DeviceStatusError",
+    "check_device_status",
+    "device_status",
+    "reset_device_status",
+    "watchdog_selftest",
+    "can_use_cute_qkvpacked",
+    "can_use_cute_window_attention",
+    "can_use_triton_adaln",
+    "can_use_triton_gelu",
+    "can_use_triton_layout",
 ]

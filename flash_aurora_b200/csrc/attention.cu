@@ -1898,9 +1898,9 @@ int* status_ptr() {
   return ptr;
 }
 
-int run(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const void* q, const void* k,
-        const void* v, void* out, const int64_t* strides, const uint8_t* mask_u8,
-        const uint8_t* group_ids, int64_t nW, float scale, unsigned flags, void* stream) {
+int validate(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const void* q, const void* k,
+             const void* v, const void* out, const int64_t* strides, bool has_mask_u8, bool has_group_ids,
+             int64_t nW, unsigned flags) {
   FA_REQUIRE(precision == FA_ATTN_BF16 || precision == FA_ATTN_FP32_3XTF32, FA_ERR_INVALID,
              "precision must be FA_ATTN_BF16 or FA_ATTN_FP32_3XTF32");
   FA_REQUIRE((flags & ~(unsigned)FA_ATTN_FLAG_REGIONS_FIT) == 0, FA_ERR_INVALID, "unknown attention flags");
@@ -1909,11 +1909,10 @@ int run(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const voi
   FA_REQUIRE((q && k && v && out) || Bwin == 0, FA_ERR_INVALID, "null tensor pointer");
   FA_REQUIRE(Dh == 64, FA_ERR_UNSUPPORTED, "window attention supports head_dim 64");
   FA_REQUIRE(N <= kMaxN, FA_ERR_UNSUPPORTED, "window attention supports N <= 144 tokens");
-  FA_REQUIRE(!(mask_u8 && group_ids), FA_ERR_INVALID, "pass at most one of mask_u8 / group_ids");
-  FA_REQUIRE(!(mask_u8 || group_ids) || nW >= 1, FA_ERR_INVALID, "nW must be >= 1 with a mask");
+  FA_REQUIRE(!(has_mask_u8 && has_group_ids), FA_ERR_INVALID, "pass at most one of mask_u8 / group_ids");
+  FA_REQUIRE(!(has_mask_u8 || has_group_ids) || nW >= 1, FA_ERR_INVALID, "nW must be >= 1 with a mask");
   FA_REQUIRE(Bwin * H < ((int64_t)1 << 31), FA_ERR_INVALID, "too many (window, head) tiles");
   if (Bwin == 0) return FA_OK;
-  FA_REQUIRE(q && k && v && out, FA_ERR_INVALID, "null tensor pointer");
   const bool f32 = precision == FA_ATTN_FP32_3XTF32;
   const int64_t es = f32 ? 4 : 2;
   const void* ptrs[3] = {q, k, v};
@@ -1925,8 +1924,17 @@ int run(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const voi
   }
   FA_REQUIRE((reinterpret_cast<uintptr_t>(out) & (f32 ? 7 : 3)) == 0 && strides[11] % 2 == 0, FA_ERR_INVALID,
              "out must be 8-byte (fp32) / 4-byte (bf16) aligned with even token stride");
+  return FA_OK;
+}
+
+int run(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const void* q, const void* k,
+        const void* v, void* out, const int64_t* strides, const uint8_t* mask_u8,
+        const uint8_t* group_ids, int64_t nW, float scale, unsigned flags, void* stream) {
+  int rc = validate(precision, Bwin, H, N, Dh, q, k, v, out, strides, mask_u8 != nullptr, group_ids != nullptr,
+                    nW, flags);
+  if (rc != FA_OK || Bwin == 0) return rc;
+  const bool f32 = precision == FA_ATTN_FP32_3XTF32;
   CUtensorMap mq, mk, mv;
-  int rc;
   if ((rc = make_map(&mq, q, f32, Bwin, H, N, strides + 0)) != FA_OK) return rc;
   if ((rc = make_map(&mk, k, f32, Bwin, H, N, strides + 3)) != FA_OK) return rc;
   if ((rc = make_map(&mv, v, f32, Bwin, H, N, strides + 6)) != FA_OK) return rc;

@@ -28,6 +28,12 @@ struct Params {
 
 int* status_ptr();
 
+// Argument checks of run() (shapes, precision, flags, pointers, strides, alignment), without
+// launching anything: FA_OK or the status run() would return for these arguments.
+int validate(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh, const void* q, const void* k,
+             const void* v, const void* out, const int64_t* strides, bool has_mask_u8, bool has_group_ids,
+             int64_t nW, unsigned flags);
+
 // Window attention on (Bwin, H, N, Dh) tensors with element strides {q, k, v, out} x
 // {window, head, token}; at most one of mask_u8 (nW, N, N) / group_ids (nW, N). Host entry of the
 // kernels in attention.cu; allocates nothing.

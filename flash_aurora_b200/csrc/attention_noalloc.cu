@@ -29,7 +29,9 @@ std::mutex g_mu;
 uint8_t* g_scratch_ptr[kMaxDevices] = {};
 
 // Device address of the scratch array on the current device. The array's name is only a host
-// stand-in, so the address is looked up once per device (with that device current) and cached.
+// stand-in, so the address is looked up once per device (with that device current) and cached
+// for the life of the process. The cache does not survive cudaDeviceReset or a re-created primary
+// context: a process that resets a device must not call this entry point on it afterwards.
 int scratch_for_current_device(uint8_t** out) {
   int dev = 0;
   FA_CUDA(cudaGetDevice(&dev));
@@ -54,7 +56,13 @@ extern "C" int fa_window_attention_bias_noalloc(int precision, int64_t Bwin, int
                                                 const void* q, const void* k, const void* v, void* out,
                                                 const int64_t strides[12], const float* bias, int64_t nW,
                                                 float scale, void* stream) {
+  // Every argument is checked before the shared scratch is touched, so a rejected call leaves the
+  // previous call's packed mask as it was.
   FA_REQUIRE(nW >= 1 && N >= 1, FA_ERR_INVALID, "nW and N must be positive");
+  FA_REQUIRE(nW <= kNoAllocMaskBytes, FA_ERR_INVALID, "nW exceeds the static scratch of fa_window_attention_bias_noalloc");
+  int rc = attn::validate(precision, Bwin, H, N, Dh, q, k, v, out, strides, true, false, nW, 0u);
+  if (rc != FA_OK) return rc;
+  // N <= 144 and nW <= 4 MiB here, so the product cannot overflow.
   const int64_t mask_bytes = nW * N * N;
   FA_REQUIRE(mask_bytes <= kNoAllocMaskBytes, FA_ERR_INVALID,
              "the packed mask needs " + std::to_string(mask_bytes) + " bytes; the static scratch of "
@@ -63,7 +71,7 @@ extern "C" int fa_window_attention_bias_noalloc(int precision, int64_t Bwin, int
   if (Bwin == 0) return FA_OK;
   FA_REQUIRE(bias, FA_ERR_INVALID, "null bias pointer");
   uint8_t* mask = nullptr;
-  int rc = scratch_for_current_device(&mask);
+  rc = scratch_for_current_device(&mask);
   if (rc != FA_OK) return rc;
   // Every byte the attention kernel reads (the first nW*N*N) is rewritten here, so no clearing of
   // the previous call's contents is needed.

@@ -8,6 +8,9 @@ copies use the copy engines, not the SMs, so they can run under the neighbouring
 stream while step ``i`` computes, and step ``i``'s download runs on another copy stream while
 step ``i + 1`` computes. Every step still moves its own input and output across PCIe; only the
 waiting is removed. Ordering is by CUDA events only; the host never blocks inside ``run``.
+:meth:`HostPipeline.wait` is the sync point: it blocks until the last download has landed and
+then checks the kernels' device status words (a pipeline wait that gave up inside a kernel is
+reported there, not by the launch), raising :class:`~flash_aurora_b200.status.DeviceStatusError`.
 """
 
 from __future__ import annotations
@@ -36,6 +39,7 @@ class HostPipeline:
         self.up = torch.cuda.Stream(self.device)
         self.down = torch.cuda.Stream(self.device)
         self._bufs: list[torch.Tensor] = []
+        self._last: torch.cuda.Event | None = None
 
     def _buffers(self, like: torch.Tensor) -> list[torch.Tensor]:
         if not self._bufs or self._bufs[0].shape != like.shape or self._bufs[0].dtype != like.dtype:
@@ -85,3 +89,14 @@ class HostPipeline:
         # The caller's stream ends after the last download, so events recorded on it after
         # run() returns bracket all the copies.
         compute.wait_event(last_down)
+        self._last = last_down
+
+    def wait(self, check_status: bool = True) -> None:
+        """Block until the outputs of the last :meth:`run` are in host memory; then, with
+        ``check_status``, raise if a kernel recorded a device-side failure meanwhile."""
+        if self._last is not None:
+            self._last.synchronize()
+        if check_status:
+            from .status import check_device_status
+
+            check_device_status(self.device)

@@ -44,6 +44,7 @@ from .adaln import (
     unmerge_adaptive_layernorm_film_add_residual_band,
 )
 from . import _lib
+from . import recorder as _rec
 from .activation import gelu_erf
 from .linear import linear_bias_act
 from .sharding import BandContext
@@ -227,6 +228,9 @@ class Swin3DTransformerBlock(nn.Module):
             sh1, sc1 = self.norm1.modulation(c)
             sh2, sc2 = self.norm2.modulation(c)
         eps = float(self.norm1.ln.eps)
+        # Algorithmic sizes of this call, for the optional step recorder (recorder.py): L tokens,
+        # T window slots (pads included), activation element size e.
+        e = 2 if bf16 else 4
         with _matmul_tf32(self.precision == "tf32"):
             x5 = x.view(B, C, H, W, D)
             if windows is not None:
@@ -234,17 +238,28 @@ class Swin3DTransformerBlock(nn.Module):
                     raise ValueError("prepartitioned windows are not used with latitude bands")
                 xw = windows
             elif band is None:
+                ev = _rec.begin()
                 xw = roll_pad_partition_windows(x5, res, self.window_size, self.shift_size, out_dtype=act)
+                _rec.end("partition", ev, L * D * 4 * B + xw.numel() * e)
             else:
                 halo = band.halo_forward(x5, ss[1]) if ss[1] else None
                 xw = roll_pad_partition_windows_band(x5, halo, field_res, self.window_size, self.shift_size,
                                                      out_dtype=act)
+            T = xw.shape[0] * xw.shape[1]
             wq, bq = self._w(self.attn.qkv, bf16)
+            ev = _rec.begin()
             qkv = F.linear(xw, wq, bq)
+            _rec.end("qkv_gemm", ev, (T * D + 3 * D * D + 3 * T * D) * e, 2 * T * D * 3 * D)
+            ev = _rec.begin()
             a = window_attn_fwd_cute_qkvpacked(qkv, heads, group_ids=gids, output_layout="bnc")
+            Nw = xw.shape[1]
+            _rec.end("attention", ev, 4 * T * D * e, 4 * xw.shape[0] * heads * Nw * Nw * (D // heads))
             wp, bp = self._w(self.attn.proj, bf16)
+            ev = _rec.begin()
             a = F.linear(a, wp, bp)
+            _rec.end("proj_gemm", ev, (2 * T * D + D * D) * e, 2 * T * D * D)
             x1_bf16 = torch.empty(B, L, D, device=x.device, dtype=torch.bfloat16) if bf16 else None
+            ev = _rec.begin()
             if band is None:
                 x1 = unmerge_adaptive_layernorm_film_add_residual(
                     a, x, sc1, sh1, res, self.window_size, self.shift_size, float(self.norm1.scale_bias), eps,
@@ -258,23 +273,35 @@ class Swin3DTransformerBlock(nn.Module):
                 x1 = unmerge_adaptive_layernorm_film_add_residual_band(
                     a, halo_in, x, sc1, sh1, res, field_res, self.window_size, self.shift_size,
                     float(self.norm1.scale_bias), eps, out_bf16=x1_bf16)
+            # windows (non-pad tokens) + fp32 residual read, fp32 output (+ bf16 copy) written
+            _rec.end("adaln1_unmerge", ev, B * L * D * (e + 4 + 4 + (2 if bf16 else 0)))
             w1, b1 = self._w(self.mlp.fc1, bf16)
+            hid = w1.shape[0]
+            ev = _rec.begin()
             if bf16 and b1 is not None and w1.shape[0] % 256 == 0 and w1.shape[1] % 64 == 0:
                 # fc1 + bias + GELU in one tensor-core kernel (GELU on the fp32 sum).
                 h = linear_bias_act(x1_bf16, w1, b1, act="gelu")
             else:
                 h = F.linear(x1_bf16 if bf16 else x1, w1, b1)
                 h = gelu_erf(h, inplace=True)
+            _rec.end("fc1_gelu_gemm", ev, (B * L * D + hid * D + B * L * hid) * e, 2 * B * L * D * hid)
             w2, b2 = self._w(self.mlp.fc2, bf16)
+            ev = _rec.begin()
             h = F.linear(h, w2, b2)
+            _rec.end("fc2_gemm", ev, (B * L * hid + hid * D + B * L * D) * e, 2 * B * L * D * hid)
+            ev = _rec.begin()
             if next_windows is not None:
                 if band is not None:
                     raise ValueError("next-block windows are not produced with latitude bands")
                 next_shift, buf = next_windows
-                return adaptive_layernorm_film_add_residual_partition(
+                y = adaptive_layernorm_film_add_residual_partition(
                     x1, h, sc2, sh2, res, self.window_size, next_shift, buf, float(self.norm2.scale_bias), eps)
-            return adaptive_layernorm_film_add_residual_forward(
+                _rec.end("adaln2_partition", ev, B * L * D * (e + 4 + 4 + e))
+                return y
+            y = adaptive_layernorm_film_add_residual_forward(
                 x1, h, sc2, sh2, float(self.norm2.scale_bias), eps, output_fp32=True)
+            _rec.end("adaln2", ev, B * L * D * (e + 4 + 4))
+            return y
 
 
 class PatchMerging3D(nn.Module):

@@ -25,6 +25,7 @@ import numpy as np
 import torch
 
 from . import _lib
+from .recorder import KernelRecorder
 from .util import window_geometry
 
 __all__ = [
@@ -39,28 +40,9 @@ __all__ = [
 WINDOW_ATTN_MASK_THRESHOLD = -50.0
 
 
-class KernelRecorder:
-    """Optional launch recorder for benchmarks: when installed with :func:`set_recorder`, every
-    attention launch is bracketed by CUDA events on its stream and its algorithmic bytes and
-    FLOPs are recorded (Q, K, V read + O written; 4 * Bwin * H * N^2 * Dh FLOPs)."""
-
-    def __init__(self) -> None:
-        self.records: list[tuple[torch.cuda.Event, torch.cuda.Event, int, int]] = []
-
-    def totals(self) -> tuple[float, int, int, int]:
-        """(milliseconds, bytes, flops, launches) summed over the recorded launches."""
-        ms = sum(a.elapsed_time(b) for a, b, _, _ in self.records)
-        return ms, sum(r[2] for r in self.records), sum(r[3] for r in self.records), len(self.records)
-
-    def by_shape(self) -> list[tuple[int, int, float]]:
-        """(bytes per launch, launches, average milliseconds) per distinct launch size, largest
-        first: the per-stage view of the same launches."""
-        acc: dict[int, list[float]] = {}
-        for a, b, nbytes, _ in self.records:
-            acc.setdefault(nbytes, []).append(a.elapsed_time(b))
-        return [(nb, len(v), sum(v) / len(v)) for nb, v in sorted(acc.items(), key=lambda kv: -kv[0])]
-
-
+# Optional launch recorder for benchmarks: when installed with set_recorder, every packed-QKV
+# attention launch is bracketed by CUDA events on its stream, with its algorithmic bytes and FLOPs
+# (Q, K, V read + O written; 4 * Bwin * H * N^2 * Dh FLOPs).
 _RECORDER: Optional[KernelRecorder] = None
 
 

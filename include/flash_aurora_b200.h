@@ -244,13 +244,15 @@ int fa_window_attention_qkvpacked(int precision, int64_t Bwin, int64_t N, int64_
                                   float scale, unsigned flags, void* stream);
 
 /*
- * fa_window_attention with a float bias (nW, N, N) (bias < -50 means masked, as upstream) that
- * allocates no device memory. No counterpart in the reference: it exists for callers that cannot
+ * fa_window_attention with a float bias (bias < -50 means masked, as upstream), a contiguous
+ * row-major fp32 (nW, N, N) array (there is no stride argument), that allocates no device memory. No counterpart in the reference: it exists for callers that cannot
  * call cudaMalloc (a host that owns the memory pool, a plugin forbidden to allocate, a loop that must
  * not allocate after start-up). The packed mask goes to a static 4 MiB device array of this
  * library, so nW * N * N must be <= 4194304 (larger sizes return FA_ERR_INVALID). The array's
  * device address is looked up on the first call on each device (call it once before any stream
- * capture). All calls share the array: calls that overlap on the GPU (other streams, other host
+ * capture) and cached for the process; after cudaDeviceReset the cached address is stale, so do
+ * not call this entry point on a device that was reset. Every argument is checked before the
+ * array is written. All calls share the array: calls that overlap on the GPU (other streams, other host
  * threads) race on it; serialise them. The caller still passes q, k, v, out and bias.
  */
 int fa_window_attention_bias_noalloc(int precision, int64_t Bwin, int64_t H, int64_t N, int64_t Dh,
@@ -276,6 +278,22 @@ int fa_layernorm_affine(const void* x, int x_dtype, const void* residual, const 
  */
 int fa_attention_status(int* status_out);
 int fa_attention_status_reset(void* stream);
+
+/* Device status codes with a fixed meaning (the other non-zero codes name the bounded wait of a
+ * kernel that gave up). */
+enum {
+  FA_STATUS_REGIONS_BROKEN = 28,      /* region ids tagged FA_ATTN_FLAG_REGIONS_FIT did not fit */
+  FA_STATUS_WATCHDOG_SELFTEST = 90    /* written by fa_watchdog_selftest */
+};
+
+/*
+ * Self-test of the bounded device-side waits (no counterpart in the reference): launches one warp
+ * that waits, with a limit of timeout_ns (1 us .. 100 ms), on an mbarrier nothing arrives on. The
+ * wait gives up, the kernel writes FA_STATUS_WATCHDOG_SELFTEST into the attention status word and
+ * returns; nothing faults and the context stays usable. A host uses it to check that its status
+ * polling (fa_attention_status after a sync point) sees a wait that expired.
+ */
+int fa_watchdog_selftest(int64_t timeout_ns, void* stream);
 
 #ifdef __cplusplus
 }

@@ -170,9 +170,14 @@ def encoder_specs(patch_res, num_layers):
 
 def backbone_forward(x, lead_time: timedelta, patch_res, p, *, embed_dim, encoder_depths,
                      encoder_num_heads, decoder_depths, decoder_num_heads, window_size,
-                     bf16_mixed: bool = False):
+                     bf16_mixed: bool = False, trace: dict | None = None):
     """swin3d.py:1247-1313: time embedding, encoder stages with merges, decoder stages with
-    splits, additive skips for the middle stages, concatenation with the first skip at the end."""
+    splits, additive skips for the middle stages, concatenation with the first skip at the end.
+
+    ``trace``: when a dict, it receives the stage outputs under the names upstream's
+    error-accumulation trace uses (benchmark/bench_backbone_error_accum.py:180-216):
+    ``enc{i}_out`` after each encoder stage (and its merge), ``dec0_out``, ``dec{i}_skip_add``
+    for the middle decoder stages and ``dec{n-1}_concat`` for the last."""
     ws = tuple(window_size)
     n_enc, n_dec = len(encoder_depths), len(decoder_depths)
     all_res, padded = encoder_specs(patch_res, n_enc)
@@ -195,6 +200,8 @@ def backbone_forward(x, lead_time: timedelta, patch_res, p, *, embed_dim, encode
         skips.append(x)
         if i < n_enc - 1:
             x = patch_merge(x, all_res[i], p, f"encoder_layers.{i}.downsample.")
+        if trace is not None:
+            trace[f"enc{i}_out"] = x
     for i in range(n_dec):
         index = n_dec - i - 1
         x = run_layer(x, "decoder", i, decoder_depths[i], decoder_num_heads[i], all_res[index])
@@ -202,8 +209,14 @@ def backbone_forward(x, lead_time: timedelta, patch_res, p, *, embed_dim, encode
             x = patch_split(x, all_res[index], padded[index - 1], p, f"decoder_layers.{i}.upsample.")
         if 0 < i < n_dec - 1:
             x = x + skips[index - 1]
+            tag = f"dec{i}_skip_add"
         elif i == n_dec - 1:
             x = torch.cat([x, skips[0]], dim=-1)
+            tag = f"dec{i}_concat"
+        else:
+            tag = f"dec{i}_out"
+        if trace is not None:
+            trace[tag] = x
     return x
 
 

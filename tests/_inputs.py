@@ -19,6 +19,18 @@ BACKBONE_SMALL = dict(
     decoder_depths=(2, 2, 2), decoder_num_heads=(8, 4, 2), window=(2, 6, 12),
     patch_res=(4, 30, 60), seed=11,
 )
+# Config 4 of the benchmark plan: the era5-shape backbone (48 blocks, latent grid (4,180,360)).
+BACKBONE_CONFIG4 = dict(
+    embed_dim=512, encoder_depths=(6, 10, 8), encoder_num_heads=(8, 16, 32),
+    decoder_depths=(8, 10, 6), decoder_num_heads=(32, 16, 8), window=(2, 6, 12),
+    patch_res=(4, 180, 360), seed=2024,
+)
+# Stage outputs recorded along the backbone, named as upstream's error-accumulation trace names
+# them (benchmark/bench_backbone_error_accum.py:180-216): each encoder stage after its patch
+# merge, the first decoder stage, the additive-skip sum of the middle one and the final
+# concatenation (the backbone output).
+TRACE_POINTS = ("enc0_out", "enc1_out", "enc2_out", "dec0_out", "dec1_skip_add", "dec2_concat")
+TRACE_ROWS = 32
 
 
 def init_params(shapes: dict, seed: int, weight_std: float = 0.02, bias_std: float = 0.0) -> dict:
@@ -66,6 +78,24 @@ def checksums(t: torch.Tensor) -> np.ndarray:
     d = t.double()
     return np.array([d.sum().item(), d.abs().sum().item(), (d * d).sum().item(),
                      d.max().item(), d.min().item()], dtype=np.float64)
+
+
+def config4_inputs(shapes: dict):
+    """Config-4 weights (``init_params``, seed 2025) and input x ~N(0,1) (1, 259200, 512) (seed
+    2026), both drawn on the CPU."""
+    cfg = BACKBONE_CONFIG4
+    params = init_params(shapes, seed=cfg["seed"] + 1)
+    C, H, W = cfg["patch_res"]
+    g = torch.Generator().manual_seed(cfg["seed"] + 2)
+    x = torch.randn(1, C * H * W, cfg["embed_dim"], generator=g)
+    return x, params
+
+
+def trace_rows(n_tokens: int, name: str, rows: int = TRACE_ROWS) -> torch.Tensor:
+    """The sorted token rows sampled at trace point ``name``: a fixed draw per point name."""
+    seed = sum((i + 1) * ord(ch) for i, ch in enumerate(name))
+    g = torch.Generator().manual_seed(seed)
+    return torch.randperm(n_tokens, generator=g)[:rows].sort().values
 
 
 def strided_sample(t: torch.Tensor, n: int = 4096) -> np.ndarray:

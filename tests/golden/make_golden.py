@@ -1,8 +1,8 @@
 """Generate the golden fixtures under ``tests/golden/`` from the upstream Flash-Aurora code.
 
-Run in a container that has the upstream source tree (default ``/root/reference``)::
+Run in a container that has the upstream source tree::
 
-    python tests/golden/make_golden.py [--reference /path/to/Flash-Aurora]
+    python tests/golden/make_golden.py --reference /path/to/Flash-Aurora [--only NAME ...]
 
 It imports the upstream PyTorch modules unmodified (through ``_reference_shim``), runs them on
 CPU in FP32 and writes compact ``.npz`` fixtures:
@@ -21,6 +21,12 @@ CPU in FP32 and writes compact ``.npz`` fixtures:
                       regenerated from the seed by ``tests/_inputs.py``.
 ``backbone_small.npz`` upstream ``Swin3DTransformerBackbone`` with odd stage sizes: output
                       checksums, a strided sample, and the upstream ``state_dict`` key list.
+``backbone_config4.npz`` upstream backbone at config 4 (embed 512, depths (6,10,8)/(8,10,6),
+                      grid (4,180,360), 48 blocks) in FP32: at each stage output of upstream's
+                      error-accumulation trace, full-tensor checksums and 32 sampled token rows;
+                      plus the drift of the oracle's ``bf16_mixed`` emulation (bf16 rounding
+                      where upstream's tier rounds) against it, over the full tensors. Takes a
+                      few minutes on 8 host cores.
 
 The upstream default init zeroes the AdaLN modulation (film.py:45-48), which would make every
 block an identity map; all Linear weights are therefore re-drawn ~N(0, 0.02) with zero biases
@@ -40,16 +46,21 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 sys.path.insert(0, os.path.dirname(HERE))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
 import _reference_shim  # noqa: E402
 from _inputs import (  # noqa: E402
+    BACKBONE_CONFIG4,
     BACKBONE_SMALL,
     BLOCK_CONFIG1,
+    TRACE_POINTS,
     BLOCK_SMALL,
     checksums,
     config1_inputs,
+    config4_inputs,
     init_params,
     strided_sample,
+    trace_rows,
 )
 
 LAYOUT_CASES = [
@@ -231,10 +242,79 @@ def _backbone_small(swin3d):
     }
 
 
+def _diff(ref: torch.Tensor, cand: torch.Tensor) -> tuple[float, float]:
+    """(relative L2, cosine similarity) in float64, as upstream's trace reports them
+    (benchmark/bench_backbone_error_accum.py:117-132)."""
+    r, c = ref.double().reshape(-1), cand.double().reshape(-1)
+    rn = r.norm().item()
+    return (c - r).norm().item() / rn, torch.dot(r, c).item() / (rn * c.norm().item())
+
+
+def _backbone_config4(swin3d):
+    """Upstream FP32 backbone at config 4 with the stage outputs captured by forward-pre-hooks
+    on the stage modules (the input of each following stage is the previous stage's traced
+    output), then the oracle's bf16_mixed emulation on the same inputs for the tier drift."""
+    import time
+
+    from oracle import block as OB
+
+    cfg = BACKBONE_CONFIG4
+    bb = swin3d.Swin3DTransformerBackbone(
+        embed_dim=cfg["embed_dim"], encoder_depths=cfg["encoder_depths"],
+        encoder_num_heads=cfg["encoder_num_heads"], decoder_depths=cfg["decoder_depths"],
+        decoder_num_heads=cfg["decoder_num_heads"], window_size=cfg["window"],
+    ).eval()
+    shapes = {k: tuple(v.shape) for k, v in bb.state_dict().items()}
+    x, sd = config4_inputs(shapes)
+    bb.load_state_dict(sd)
+    stages = list(bb.encoder_layers) + list(bb.decoder_layers)
+    points: dict = {}
+
+    def pre_hook(name):
+        def hook(_mod, args):
+            points[name] = args[0].detach().clone()
+        return hook
+
+    hooks = [stages[i + 1].register_forward_pre_hook(pre_hook(name))
+             for i, name in enumerate(TRACE_POINTS[:-1])]
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        y = bb(x, lead_time=timedelta(hours=6), rollout_step=0, patch_res=cfg["patch_res"])
+    for h in hooks:
+        h.remove()
+    points[TRACE_POINTS[-1]] = y
+    print(f"upstream fp32 config-4 backbone: {time.perf_counter() - t0:.0f} s")
+    del bb
+    emu: dict = {}
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        OB.backbone_forward(x, timedelta(hours=6), cfg["patch_res"], sd, embed_dim=cfg["embed_dim"],
+                            encoder_depths=cfg["encoder_depths"], encoder_num_heads=cfg["encoder_num_heads"],
+                            decoder_depths=cfg["decoder_depths"], decoder_num_heads=cfg["decoder_num_heads"],
+                            window_size=cfg["window"], bf16_mixed=True, trace=emu)
+    print(f"oracle bf16_mixed emulation: {time.perf_counter() - t0:.0f} s")
+    out = {"x_checksums": checksums(x), "points": np.array(TRACE_POINTS)}
+    for name in TRACE_POINTS:
+        t = points[name].reshape(-1, points[name].shape[-1])
+        e = emu[name].reshape(t.shape)
+        rows = trace_rows(t.shape[0], name)
+        rel, cos = _diff(t, e)
+        rel_rows, _ = _diff(t[rows], e[rows])
+        out.update({
+            f"{name}/checksums": checksums(t), f"{name}/shape": np.array(points[name].shape),
+            f"{name}/row_index": rows.numpy(), f"{name}/rows": t[rows].numpy(),
+            f"{name}/emulated_bf16_mixed": np.array([rel, cos, rel_rows]),
+        })
+        print(f"{name:>14}: emulated bf16_mixed drift rel-L2 {rel:.3e} (sampled rows {rel_rows:.3e}), "
+              f"cos {cos:.8f}")
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of the upstream Flash-Aurora source tree")
     ap.add_argument("--out", default=HERE)
+    ap.add_argument("--only", nargs="*", default=None, help="fixture file names to (re)generate")
     args = ap.parse_args()
     _reference_shim.install(args.reference)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
@@ -248,8 +328,11 @@ def main() -> None:
         "block_small.npz": lambda: _block_small(swin3d),
         "block_config1.npz": lambda: _block_config1(swin3d),
         "backbone_small.npz": lambda: _backbone_small(swin3d),
+        "backbone_config4.npz": lambda: _backbone_config4(swin3d),
     }
     for fname, fn in jobs.items():
+        if args.only is not None and fname not in args.only:
+            continue
         data = fn()
         path = os.path.join(args.out, fname)
         np.savez_compressed(path, **data)

@@ -82,7 +82,16 @@ def test_workspace_pool_reuses_buffers():
     b = pool.get("k", (2, 3), device="cpu", dtype=torch.float32)
     c = pool.get("k", (2, 4), device="cpu", dtype=torch.float32)
     assert a.data_ptr() == b.data_ptr() and c.shape == (2, 4)
+    # A smaller request of another dtype reuses the arena; a larger one grows it.
+    d = pool.get("k", (3,), device="cpu", dtype=torch.bfloat16)
+    assert d.data_ptr() == a.data_ptr() and d.dtype == torch.bfloat16
+    big = pool.get("k", (1000,), device="cpu", dtype=torch.float32)
+    assert big.numel() == 1000 and pool.nbytes() >= 4000
+    other = pool.get("other", (2, 3), device="cpu", dtype=torch.float32)
+    assert other.data_ptr() != big.data_ptr()
+    assert pool.get("k", (0, 5), device="cpu", dtype=torch.float32).shape == (0, 5)
     pool.clear()
+    assert pool.nbytes() == 0
 
 
 def test_lead_time_expansion_matches_oracle():
@@ -126,3 +135,38 @@ def test_maybe_adjust_windows_matches_oracle():
         assert maybe_adjust_windows(ws, ss, res) == OL.maybe_adjust_windows(ws, ss, res)
     with pytest.raises(AssertionError, match="Window size must be positive"):
         maybe_adjust_windows((2, 6, 12), (1, 3, 6), (0, 6, 12))
+
+
+def test_gating_predicates(monkeypatch):
+    """The upstream ``can_use_*`` predicates (custom_op_paths.py:501-579) under their names: the
+    upstream conditions plus the B200 kernels' own limits. On a CPU tensor every one is False;
+    with the device check faked to pass, each condition is checked in turn."""
+    from flash_aurora_b200 import custom_op_paths as cop
+
+    x = torch.zeros(2, 144, 3 * 8 * 64)
+    assert not cop.b200_available(x)
+    assert not cop.can_use_triton_layout(x, enabled=True)
+    assert not cop.can_use_cute_qkvpacked(x, num_heads=8, head_dim=64, cute_enabled=True, training=False,
+                                          attn_dropout=0.0)
+    monkeypatch.setattr(cop, "b200_available", lambda t: True)
+    assert cop.can_use_triton_layout(x, enabled=True)
+    assert not cop.can_use_triton_layout(x, enabled=False)
+    assert not cop.can_use_triton_layout(x.half(), enabled=True)
+    assert cop.can_use_triton_adaln(x, enabled=True, training=False, drop_path_is_identity=True)
+    assert not cop.can_use_triton_adaln(x.bfloat16(), enabled=True, training=False, drop_path_is_identity=True)
+    assert not cop.can_use_triton_adaln(x, enabled=True, training=True, drop_path_is_identity=True)
+    assert cop.can_use_triton_gelu(x.bfloat16(), enabled=True, training=False, drop_p=0.0)
+    assert not cop.can_use_triton_gelu(x, enabled=True, training=False, drop_p=0.1)
+    ok = dict(num_heads=8, head_dim=64, cute_enabled=True, training=False, attn_dropout=0.0)
+    with torch.no_grad():
+        assert cop.can_use_cute_qkvpacked(x, **ok)
+        assert cop.can_use_cute_qkvpacked(x.bfloat16(), **ok)
+        assert not cop.can_use_cute_qkvpacked(x, **{**ok, "head_dim": 32})  # the kernels need 64
+        assert not cop.can_use_cute_qkvpacked(x, **{**ok, "num_heads": 4})  # last dim != 3 * H * Dh
+        assert not cop.can_use_cute_qkvpacked(x[:, :, : 3 * 8 * 64 - 1], **ok)
+        assert not cop.can_use_cute_qkvpacked(x.transpose(0, 1), **ok)  # not contiguous
+        assert not cop.can_use_cute_qkvpacked(torch.zeros(2, 160, 3 * 8 * 64), **ok)  # N > 144
+        assert not cop.can_use_cute_qkvpacked(x, **{**ok, "attn_dropout": 0.1})
+        assert cop.can_use_cute_window_attention(torch.zeros(2, 8, 144, 64), enabled=True, training=False,
+                                                 attn_dropout=0.0)
+    assert not cop.can_use_cute_qkvpacked(x, **ok)  # grad enabled

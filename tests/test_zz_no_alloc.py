@@ -16,6 +16,7 @@ import torch
 
 import flash_aurora_b200 as fa
 from flash_aurora_b200 import _lib
+from oracle import block as OB
 
 pytestmark = pytest.mark.gpu
 
@@ -52,10 +53,32 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls(dtype):
         want = fa.window_attn_fwd_cute(q, k, v, bias, scale_qk=scale, precision=prec)
         got = _noalloc(q, k, v, bias, code, scale)
         torch.cuda.synchronize()
-        # Same kernel on the same packed mask: the results agree exactly; the tolerance is the one
-        # the attention tests use for this precision.
+        # Same kernel on the same packed mask: the two entry points agree bit for bit.
+        assert torch.equal(got, want), f"call {call}"
+        # And against the CPU restatement of the upstream attention, within the attention tests'
+        # tolerance for this precision (relative L2).
+        ref = OB.window_attention_core(q.float().cpu(), k.float().cpu(), v.float().cpu(), bias.cpu(), scale)
         tol = 2e-2 if dtype == torch.bfloat16 else 1e-5
-        torch.testing.assert_close(got.float(), want.float(), rtol=tol, atol=tol, msg=f"call {call}")
+        assert OB.relative_l2(got.float().cpu(), ref) <= tol, f"call {call}"
+
+
+def test_noalloc_checks_arguments_before_writing_the_scratch():
+    """A call rejected for its shape returns the error and leaves the scratch alone: a valid call
+    before and after it gives the same result."""
+    Bwin, H, N, Dh, nW = 4, 2, 144, 64, 4
+    g = torch.Generator().manual_seed(3)
+    q, k, v = ((torch.randn(Bwin, H, N, Dh, generator=g)).bfloat16().cuda() for _ in range(3))
+    bias = _bias(nW, N, 5).cuda()
+    first = _noalloc(q, k, v, bias, _lib.FA_ATTN_BF16, 0.125)
+    big = torch.zeros(1, 1, 160, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="N <= 144"):
+        _noalloc(big, big, big, torch.full((1, 160, 160), -100.0, device="cuda"), _lib.FA_ATTN_BF16, 0.125)
+    with pytest.raises(ValueError, match="head_dim"):
+        odd = torch.zeros(1, 1, N, 32, device="cuda", dtype=torch.bfloat16)
+        _noalloc(odd, odd, odd, bias, _lib.FA_ATTN_BF16, 0.125)
+    again = _noalloc(q, k, v, bias, _lib.FA_ATTN_BF16, 0.125)
+    torch.cuda.synchronize()
+    assert torch.equal(first, again)
 
 
 def test_noalloc_rejects_masks_beyond_the_static_scratch():
