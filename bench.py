@@ -1,6 +1,6 @@
 """Benchmark of the Swin3D backbone hot path on B200.
 
-Default (what the driver runs): the era5-shape Swin3D U-net backbone forward (
+Default (what the driver runs): the era5-shape Swin3D U-net backbone forward (benchmark config 4:
 embed 512, encoder depths (6,10,8) / decoder (8,10,6), heads (8,16,32)/(32,16,8), window (2,6,12),
 latent grid (4,180,360), batch 1) in the ``bf16_mixed`` tier, random init ~N(0, 0.02), synthetic
 ~N(0,1) input. One step = one backbone forward. Metric: ms/step (lower is better).
@@ -10,20 +10,30 @@ latent grid (4,180,360), batch 1) in the ``bf16_mixed`` tier, random init ~N(0, 
 * ``e2e``        the same steps through the public API from pinned host memory: every step's H2D
                  of its input and D2H of its full output are inside the timed region, overlapped
                  with the neighbouring steps' compute by ``flash_aurora_b200.pipeline.HostPipeline``.
-* ``roofline``   the window-attention kernel (the hot kernel of this library), from CUDA events
-                 around every attention launch inside the timed region: algorithmic bytes
-                 (Q, K, V read + O written, bf16) / kernel time, against the measured HBM peak.
+* ``step_breakdown`` one eager pass of the same steps with CUDA events around every operator of
+                 every block (partition, QKV GEMM, attention, proj GEMM, AdaLN1, fc1 + GELU, fc2,
+                 AdaLN2): per operator its time per step, share, and achieved TFLOP/s or GB/s
+                 against the measured peaks (GEMMs against the sustained bf16 figure, since they
+                 run inside a long step). Library GEMMs are included.
+* ``roofline``   the dominant kernel of this library in that breakdown, in the contract's form.
+* ``gpu_launches`` kernel launches of this library inside the timed region, counted from the nodes
+                 of the captured graph (``launches_per_step`` also gives the library ones).
 * ``cpu_baseline`` the CPU oracle (upstream FP32 algorithm restated in torch-CPU) on one shifted
                  block per stage, extrapolated to the 48-block step (rank 0, N = 1 only).
+* ``same_box_bars`` the stock PyTorch path on the same GPU, for comparison: config-2 attention
+                 through ``scaled_dot_product_attention`` with the float mask, and one stage-1
+                 block in eager PyTorch under bf16 autocast.
 
 Multi-GPU (``torchrun --nproc-per-node N``): every rank runs its own backbone step on its own
 input (independent ensemble members, no data-path collective): weak scaling, replicas. The
-line also carries ``sharded_config5``: BASELINE config 5 (a (4,360,720) x 512 Swin3D stage of
+line also carries ``sharded_config5``: benchmark config 5 (a (4,360,720) x 512 Swin3D stage of
 10 blocks) split into latitude bands across the N ranks with the NCCL point-to-point halo
-exchange, strong scaling (``--no-sharded`` skips it; ``--workload sharded`` runs it alone).
+exchange, strong scaling, with a parity check of the banded result against the whole field run on
+one GPU (``--no-sharded`` skips it; ``--workload sharded`` runs it alone).
 
 ``--impl reference`` times the reference algorithm on the host CPU instead (the CPU oracle, see
-above; rank 0 only) and prints the same metric.
+above; rank 0 only) and prints the same metric. It cannot run a 48-block step within minutes, so
+each timed "step" is one block and the line says so (``extrapolated``, ``blocks_timed``).
 """
 
 from __future__ import annotations
@@ -59,6 +69,15 @@ def _peaks():
         return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     except Exception:
         return 6650.0, 1590.0, "fallback"
+
+
+def _sustained_tflops() -> tuple[float, str]:
+    """The bf16 GEMM peak under the power cap (seconds-long loop), for kernels timed in a step."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops_sustained"]), "measured sustained"
+    except Exception:
+        return 1400.0, "fallback sustained"
 
 
 class ClockSampler:
@@ -183,12 +202,22 @@ def run_reference(args) -> None:
             res, dim, heads, _ = STAGES[s]
             times[s].append(_cpu_block_ms(res, dim, heads, 7 + s))
     value = sum(statistics.mean(times[s]) * STAGES[s][3] for s in range(3))
+    blocks_timed = [len(times[s]) for s in range(3)]
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 1), "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "config4: era5 Swin3D backbone forward, 48 blocks, grid (4,180,360), batch 1",
                    "parallelism": "host CPU"},
+        # A 48-block FP32 step takes tens of minutes on the host; each timed "step" of this arm is
+        # one shifted block of stage S1, S2, S3 in turn, and the value extrapolates the per-stage
+        # mean to the step's (12, 20, 16) blocks. Stage merges/splits (1.4 % of FLOPs) are not timed.
+        "extrapolated": True,
+        "step_definition": "one shifted block of one stage (S1, S2, S3 in turn), not a backbone step",
+        "blocks_timed": {"S1": blocks_timed[0], "S2": blocks_timed[1], "S3": blocks_timed[2]},
+        "block_ms": {"S1": round(statistics.mean(times[0]), 1), "S2": round(statistics.mean(times[1]), 1),
+                     "S3": round(statistics.mean(times[2]), 1)},
+        "blocks_per_step": {"S1": STAGES[0][3], "S2": STAGES[1][3], "S3": STAGES[2][3]},
         "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": "each step = one shifted block of stage S1/S2/S3 in turn on the CPU oracle "
                                    "(upstream FP32 algorithm), mean per stage x (12,20,16) blocks"},
@@ -200,8 +229,115 @@ def run_reference(args) -> None:
 # ----------------------------------------------------------------------------------------------
 # B200 arm
 # ----------------------------------------------------------------------------------------------
+# Operators of the block forward as the step recorder names them: (bound, implementation).
+OPERATORS = {
+    "partition": ("hbm", "this library: partition_kernel (first block of each stage)"),
+    "qkv_gemm": ("tensor", "cuBLAS bf16 GEMM"),
+    "attention": ("hbm", "this library: attn_tc_bf16_kernel (tcgen05)"),
+    "proj_gemm": ("tensor", "cuBLAS bf16 GEMM"),
+    "adaln1_unmerge": ("hbm", "this library: adaln_kernel (unmerge-fused, bf16 copy)"),
+    "fc1_gelu_gemm": ("tensor", "this library: gemm_bias_act_kernel<gelu> (tcgen05)"),
+    "fc2_gemm": ("tensor", "cuBLAS bf16 GEMM"),
+    "adaln2_partition": ("hbm", "this library: adaln_kernel (next-partition fused)"),
+    "adaln2": ("hbm", "this library: adaln_kernel"),
+}
+# DRAM bytes / algorithmic bytes from ncu captures of the kernel (profiles/): the attention at
+# config 2 and the fused fc1 + GELU at the config-4 stage-1 shape.
+TRAFFIC_RATIOS = {"attention": TRAFFIC_RATIO, "fc1_gelu_gemm": 0.956}
+
+
+def _is_own_kernel(name: str) -> bool:
+    """Kernels of this library live in C++ namespace ``fa`` (mangled prefix ``_ZN2fa``)."""
+    return name.startswith("_ZN2fa") or "fa::" in name
+
+
+def step_breakdown(summary: dict, step_ms: float, hbm: float, tf_sus: float, tf_kind: str, peak_kind: str) -> list:
+    rows = []
+    for kind, v in sorted(summary.items(), key=lambda kv: -kv[1]["ms_per_step"]):
+        bound, impl = OPERATORS.get(kind, ("hbm", "?"))
+        ms = v["ms_per_step"]
+        row = {"operator": kind, "impl": impl, "ms_per_step": round(ms, 3),
+               "share_of_step": round(ms / step_ms, 3) if step_ms > 0 else None,
+               "launches_per_step": round(v["launches_per_step"], 1), "bound": bound}
+        if bound == "tensor":
+            tf = v["flops_per_step"] / (ms * 1e-3) / 1e12 if ms > 0 else 0.0
+            row.update({"achieved": round(tf, 1), "unit": "TFLOP/s", "peak": tf_sus, "peak_kind": tf_kind,
+                        "frac": round(tf / tf_sus, 3)})
+        else:
+            gbs = v["bytes_per_step"] / (ms * 1e-3) / 1e9 if ms > 0 else 0.0
+            row.update({"achieved": round(gbs, 1), "unit": "GB/s", "peak": hbm, "peak_kind": peak_kind,
+                        "frac": round(gbs / hbm, 3)})
+        rows.append(row)
+    return rows
+
+
+def same_box_bars(dev) -> dict:
+    """The stock PyTorch path on this GPU: config-2 attention through SDPA with the float mask,
+    and one stage-1 shifted block in eager PyTorch under bf16 autocast (the upstream fallback
+    path's operators: roll, pad, partition, Linear, SDPA, LayerNorm), each beside this library's."""
+    import torch.nn.functional as F
+
+    import flash_aurora_b200 as fa
+    from flash_aurora_b200.swin3d import Swin3DTransformerBlock
+
+    flush = L2Flush(dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    res, ws, ss = (4, 180, 360), (2, 6, 12), (1, 3, 6)
+    Bwin, H, N, Dh = 1800, 8, 144, 64
+    qkv = (torch.randn(Bwin, N, 3 * H * Dh, device=dev, generator=g) / 8.0).bfloat16()
+    gids = fa.shifted_window_group_ids(res, ws, ss, device=dev)
+    bias = torch.where(gids[:, :, None] != gids[:, None, :], -100.0, 0.0).to(torch.bfloat16)
+    q, k, v = qkv.view(Bwin, N, 3, H, Dh).permute(2, 0, 3, 1, 4)
+    ms_sdpa = _time_launches(lambda: F.scaled_dot_product_attention(q, k, v, attn_mask=bias[:, None]), 5,
+                             flush=flush)
+    ms_own = _time_launches(lambda: fa.window_attn_fwd_cute_qkvpacked(qkv, H, group_ids=gids, output_layout="bnc"),
+                            5, flush=flush)
+    del qkv, q, k, v, bias
+    # One S1 shifted block.
+    C, Hh, W = res
+    D, heads = 512, 8
+    blk = Swin3DTransformerBlock(dim=D, num_heads=heads, time_dim=D, window_size=ws, shift_size=ss).to(dev).eval()
+    with torch.no_grad():
+        for p in blk.parameters():
+            p.normal_(0.0, 0.02, generator=g) if p.ndim == 2 else p.zero_()
+    x = torch.randn(1, C * Hh * W, D, device=dev, generator=g)
+    c = torch.randn(1, D, device=dev, generator=g)
+    mask = torch.where(gids[:, :, None] != gids[:, None, :], -100.0, 0.0)
+
+    def eager_block():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            x5 = torch.roll(x.view(1, C, Hh, W, D), shifts=(-1, -3, -6), dims=(1, 2, 3))
+            xw = x5.view(1, C // 2, 2, Hh // 6, 6, W // 12, 12, D).permute(0, 1, 3, 5, 2, 4, 6, 7).reshape(-1, N, D)
+            qkv_ = F.linear(xw, blk.attn.qkv.weight, blk.attn.qkv.bias).view(-1, N, 3, heads, Dh).permute(2, 0, 3, 1, 4)
+            a = F.scaled_dot_product_attention(qkv_[0], qkv_[1], qkv_[2], attn_mask=mask[:, None].to(qkv_.dtype))
+            a = F.linear(a.transpose(1, 2).reshape(-1, N, D), blk.attn.proj.weight, blk.attn.proj.bias).float()
+        a = a.view(1, C // 2, Hh // 6, W // 12, 2, 6, 12, D).permute(0, 1, 4, 2, 5, 3, 6, 7).reshape(1, C, Hh, W, D)
+        a = torch.roll(a, shifts=(1, 3, 6), dims=(1, 2, 3)).reshape(1, -1, D)
+        sh1, sc1 = blk.norm1.modulation(c)
+        x1 = x + F.layer_norm(a, (D,)) * sc1 + sh1
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            hdn = F.gelu(F.linear(x1, blk.mlp.fc1.weight, blk.mlp.fc1.bias))
+            hdn = F.linear(hdn, blk.mlp.fc2.weight, blk.mlp.fc2.bias)
+        sh2, sc2 = blk.norm2.modulation(c)
+        return x1 + F.layer_norm(hdn.float(), (D,)) * sc2 + sh2
+
+    with torch.no_grad():
+        ms_eager_blk = _time_launches(eager_block, 3, flush=flush)
+        ms_own_blk = _time_launches(lambda: blk(x, c, res), 3, flush=flush)
+    del blk, x, mask, flush
+    torch.cuda.empty_cache()
+    return {"attention_config2_masked_bf16": {"torch_sdpa_ms": round(ms_sdpa, 4), "this_library_ms": round(ms_own, 4),
+                                              "speedup": round(ms_sdpa / ms_own, 2)},
+            "block_s1_shifted_bf16": {"torch_eager_autocast_ms": round(ms_eager_blk, 3),
+                                      "this_library_ms": round(ms_own_blk, 3),
+                                      "speedup": round(ms_eager_blk / ms_own_blk, 2)},
+            "note": "stock PyTorch operators on the same GPU (CUDA events, L2 flushed); the reference's own "
+                    "CuTe/Triton kernels need their JIT sources at run time and are not on this box"}
+
+
 def run_b200(args) -> None:
-    from flash_aurora_b200 import window_attn as WA
+    from flash_aurora_b200 import recorder as R
+    from flash_aurora_b200.status import check_device_status
     from flash_aurora_b200.swin3d import Swin3DTransformerBackbone, init_random_weights_
 
     dist, rank, world, local = _dist()
@@ -240,16 +376,24 @@ def run_b200(args) -> None:
         clocks = sampler.stop()
         ms = e0.elapsed_time(e1) / args.steps
         ms = _max_over_ranks(dist, ms)
-        # Attention roofline: the same steps run eagerly, with CUDA events around every attention
-        # launch on its stream (per-launch events cannot be timed inside a graph).
-        rec = WA.KernelRecorder()
-        WA.set_recorder(rec)
+        check_device_status(dev)  # a kernel that gave up a bounded wait would raise here
+        try:
+            names = graphed.kernel_names()
+            own = sum(1 for n in names if _is_own_kernel(n))
+            launches = {"total": len(names), "this_library": own, "libraries": len(names) - own,
+                        "source": "kernel nodes of the captured graph replayed in the timed region"}
+        except Exception as exc:  # noqa: BLE001 - reported, not fatal
+            launches = {"error": f"graph introspection failed: {exc}"}
+        # Per-operator breakdown: the same steps run eagerly, with CUDA events around every
+        # operator of every block on the launch stream (events cannot be timed inside a graph).
+        srec = R.StepRecorder()
+        R.set_step_recorder(srec)
         for _ in range(args.steps):
             step(x)
         torch.cuda.synchronize()
-        WA.set_recorder(None)
-        attn_ms, attn_bytes, attn_flops, attn_launches = rec.totals()
-        attn_shapes = rec.by_shape()
+        R.set_step_recorder(None)
+        summary = srec.summary(args.steps)
+        attn_shapes = srec.get("attention").by_shape()
 
         # End to end from pinned host memory through the public API: every step uploads its
         # input and downloads its full output; HostPipeline overlaps those copies with the
@@ -259,25 +403,38 @@ def run_b200(args) -> None:
         out_host = [torch.empty(tuple(y.shape), dtype=y.dtype, pin_memory=True) for _ in range(2)]
         pipe = HostPipeline(graphed, dev)
         pipe.run(x_host[:1], out_host[:1])  # warm the pipeline's streams and buffers
+        pipe.wait()
         _barrier(dist)
         e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e2.record()
         pipe.run([x_host[i % 2] for i in range(args.steps)], [out_host[i % 2] for i in range(args.steps)])
         e3.record()
         _barrier(dist)
+        pipe.wait()  # outputs landed; raises on a device-side failure
         e2e_ms = _max_over_ranks(dist, e2.elapsed_time(e3) / args.steps)
         yy = y
 
     hbm, _, peak_kind = _peaks()
-    achieved = attn_bytes / (attn_ms * 1e-3) / 1e9 if attn_ms > 0 else 0.0
-    # DRAM traffic per launch: the ncu capture of config-2 launches measured
-    # dram__bytes_read + dram__bytes_write = 0.973 x the algorithmic bytes (Q, K, V once,
-    # part of O still in L2 at exit); the same ratio is applied to this step's average launch.
-    traffic = round(TRAFFIC_RATIO * attn_bytes / attn_launches) if attn_launches else None
-    # Per block: attention, unmerge+AdaLN1, GELU, AdaLN2 (fused with the next block's partition);
-    # plus the partition of the first block of each of the 6 stages.
+    tf_sus, tf_kind = _sustained_tflops()
+    rows = step_breakdown(summary, ms, hbm, tf_sus, tf_kind, peak_kind)
+    # The contract's roofline object: the dominant kernel of this library in the breakdown.
+    own_rows = [r for r in rows if r["impl"].startswith("this library")]
+    top = max(own_rows, key=lambda r: r["ms_per_step"])
+    tsum = summary[top["operator"]]
+    n_top = tsum["launches_per_step"]
+    per_launch_alg = (tsum["bytes_per_step"] / n_top) if n_top else None
+    ratio = TRAFFIC_RATIOS.get(top["operator"])
+    roofline = {"kernel": f"{top['operator']}: {top['impl']} (per-launch average over an eager pass of the same steps)",
+                "bound": top["bound"], "achieved": top["achieved"], "peak": top["peak"], "unit": top["unit"],
+                "frac": top["frac"], "peak_kind": top["peak_kind"],
+                "traffic": round(ratio * per_launch_alg) if (ratio and per_launch_alg) else None,
+                "traffic_source": "ncu DRAM bytes / algorithmic bytes of this kernel (profiles/) x this step's "
+                                  "algorithmic bytes per launch" if ratio else None,
+                "algorithmic_bytes_per_launch": round(per_launch_alg) if per_launch_alg else None,
+                "flops_per_launch": round(tsum["flops_per_step"] / n_top) if n_top else None,
+                "launches_per_step": n_top, "kernel_ms_per_step": top["ms_per_step"]}
+    attn = summary.get("attention", {})
     n_blocks = sum(CONFIG4["encoder_depths"]) + sum(CONFIG4["decoder_depths"])
-    per_step_launches = 4 * n_blocks + len(CONFIG4["encoder_depths"]) + len(CONFIG4["decoder_depths"])
     line = {
         "metric": METRIC, "value": round(ms, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": False, "scaling": "weak",
@@ -286,27 +443,26 @@ def run_b200(args) -> None:
                                "heads (8,16,32)/(32,16,8), window (2,6,12), grid (4,180,360), batch 1), bf16_mixed",
                    "global_batch": world, "parallelism": f"replicas x{world} (independent members, no collective)",
                    "l2": "inputs and per-block activations > L2 (126 MB)",
-                   "execution": "step captured once as a CUDA graph and replayed (static shapes)"},
+                   "execution": "step captured once as a CUDA graph and replayed (static shapes)",
+                   "blocks": n_blocks},
         "e2e": {"value": round(e2e_ms, 2), "unit": UNIT, "h2d_bytes_per_step": x.numel() * x.element_size(),
                 "d2h_bytes_per_step": y.numel() * y.element_size()},
-        "gpu_launches": per_step_launches * args.steps,
-        "roofline": {"kernel": "window attention (bf16, per-launch average over an eager pass of the same steps)",
-                     "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 3), "traffic": traffic,
-                     "traffic_source": "ncu config-2 capture ratio 0.973 x this step's bytes per launch",
-                     "algorithmic_bytes_per_launch": round(attn_bytes / attn_launches) if attn_launches else None,
-                     "peak_kind": peak_kind,
-                     "tflops": round(attn_flops / (attn_ms * 1e-3) / 1e12, 1) if attn_ms > 0 else None,
-                     "launches": attn_launches, "kernel_ms_per_step": round(attn_ms / args.steps, 3),
-                     # per launch size (one per backbone stage): fraction of the peak each stage reaches
-                     "by_launch_size": [{"bytes": nb, "launches": n, "ms": round(t, 4),
-                                         "frac": round(nb / (t * 1e-3) / 1e9 / hbm, 3)} for nb, n, t in attn_shapes]},
+        "gpu_launches": (launches["this_library"] * args.steps) if "this_library" in launches else None,
+        "launches_per_step": launches,
+        "roofline": roofline,
+        "step_breakdown": rows,
+        "attention_by_stage": [{"bytes": nb, "launches": n, "ms": round(t, 4),
+                                "frac": round(nb / (t * 1e-3) / 1e9 / hbm, 3)} for nb, n, t in attn_shapes],
+        "attention_tflops_in_step": round(attn["flops_per_step"] / (attn["ms_per_step"] * 1e-3) / 1e12, 1)
+        if attn.get("ms_per_step") else None,
         "clocks": clocks,
     }
     del model, x, y, yy, graphed, pipe
     torch.cuda.empty_cache()
     if not args.no_sharded:
         line["sharded_config5"] = measure_sharded(dist, rank, world, local, min(args.steps, 5), 3)
+    if rank == 0 and not args.no_bars:
+        line["same_box_bars"] = same_box_bars(dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample()
     if rank == 0:
@@ -342,33 +498,55 @@ def measure_sharded(dist, rank, world, local, steps, warmup) -> dict:
     layer = layer.to(dev).eval()
     group = dist.group.WORLD if dist is not None else None
     ctx = BandContext(cfg["field"], cfg["window"], rank, world, group=group, timeout_s=120)
-    gen = torch.Generator(device=dev).manual_seed(99 + rank)
+    # Every rank draws the same whole field and keeps its band, so the banded result can be
+    # checked against the whole field run unsharded on one GPU.
+    gen = torch.Generator(device=dev).manual_seed(99)
+    x_field = torch.randn(1, C, H, W, D, device=dev, generator=gen)
     Cb, Hb, Wb = ctx.res
-    xb = torch.randn(1, Cb * Hb * Wb, D, device=dev, generator=gen)
+    xb = x_field[:, :, ctx.h_begin:ctx.h_end].reshape(1, Cb * Hb * Wb, D).contiguous()
     c = torch.randn(1, D, device=dev, generator=torch.Generator(device=dev).manual_seed(98))
     with torch.no_grad():
+        # Parity: this rank's band of the sharded stage against the same rows of the unsharded
+        # stage (same weights, same input), reduced over the ranks.
+        y_band, _ = layer(xb, c, ctx.res, band=ctx)
+        y_full, _ = layer(x_field.reshape(1, C * H * W, D), c, cfg["field"])
+        want = y_full.view(1, C, H, W, D)[:, :, ctx.h_begin:ctx.h_end].reshape_as(y_band)
+        diff = (y_band.double() - want.double())
+        acc = torch.stack([diff.square().sum(), want.double().square().sum()])
+        mx = diff.abs().max().reshape(1)
+        if dist is not None:
+            dist.all_reduce(acc)
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        rel = float((acc[0] / acc[1]).sqrt().item())
+        parity = {"rel_l2": rel, "max_abs": float(mx.item()), "bound": 5e-3, "ok": bool(rel <= 5e-3),
+                  "against": "the same stage on the whole field, unsharded, on one GPU (same seeded weights "
+                             "and input); bf16 GEMM rounding differs with the row count"}
+        del y_full, want, diff, x_field
+        torch.cuda.empty_cache()
         for _ in range(warmup):
             y, _ = layer(xb, c, ctx.res, band=ctx)
+        ctx.wait()  # raises HaloExchangeError if a neighbour stopped answering
         _barrier(dist)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
             y, _ = layer(xb, c, ctx.res, band=ctx)
         e1.record()
+        ctx.wait()
         _barrier(dist)
     ms = _max_over_ranks(dist, e0.elapsed_time(e1) / steps)
     shifted = cfg["depth"] // 2
-    halo_fwd = C * 3 * W * D * 4 if world > 1 else 0  # fp32 rows to the previous band
+    halo_fwd = C * 3 * W * D * 2 if world > 1 else 0  # rows to the previous band, sent as bf16
     halo_back = C * 3 * W * D * 2 if world > 1 else 0  # bf16 rows to the next band
     nw = C // 2 * (H // 6) * (W // 12)
     flops_block = 2 * C * H * W * D * (3 * D + D + 8 * D) + 4 * nw * cfg["heads"] * 144 * 144 * (D // cfg["heads"])
-    del layer, xb, y
+    del layer, xb, y, y_band
     torch.cuda.empty_cache()
     return {"workload": "config5: Swin3D stage, field (4,360,720) x 512, 8 heads, 10 blocks (5 shifted), "
                         "bf16_mixed, latitude bands of window rows, NCCL P2P 3-row halo per shifted block",
             "ms_per_step": round(ms, 3), "windows_per_s": round(nw * cfg["depth"] / (ms * 1e-3), 1),
             "tflops": round(flops_block * cfg["depth"] / (ms * 1e-3) / 1e12, 1),
-            "bands": [list(b) for b in ctx.bounds], "scaling": "strong",
+            "bands": [list(b) for b in ctx.bounds], "scaling": "strong", "parity": parity,
             "halo_bytes_per_rank_per_step": shifted * (halo_fwd + halo_back), "steps": steps, "warmup": warmup}
 
 
@@ -384,7 +562,7 @@ def run_sharded(args) -> None:
 
 
 # ----------------------------------------------------------------------------------------------
-# Kernel-level workloads (BASELINE configs 2 and 3); not the driver's default line.
+# Kernel-level workloads (benchmark configs 2 and 3); not the driver's default line.
 # ----------------------------------------------------------------------------------------------
 class L2Flush:
     """Empties L2 between timed launches: writes a 256 MB buffer (twice L2), then reads another
@@ -573,6 +751,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sharded", action="store_true", help="skip the config-5 sharded-stage object")
+    ap.add_argument("--no-bars", action="store_true", help="skip the same-box stock PyTorch comparison")
     ap.add_argument("--workload", choices=["backbone", "attention", "layout_adaln", "adaln_stages", "sharded"], default="backbone")
     args = ap.parse_args()
     if args.warmup < 3:

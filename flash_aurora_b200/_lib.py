@@ -43,7 +43,7 @@ SIGNATURES = {
                                        _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
     "fa_unmerge_adaln_film": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _f32, _f32, _vp, _i32, _vp,
                                      _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
-    "fa_roll_pad_partition_band": (_i32, [_vp, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64,
+    "fa_roll_pad_partition_band": (_i32, [_vp, _vp, _i32, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64,
                                           _i32p, _i32p, _vp]),
     "fa_band_halo_extract": (_i32, [_vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
     "fa_crop_roll_unmerge_band": (_i32, [_vp, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64,

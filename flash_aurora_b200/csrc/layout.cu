@@ -22,9 +22,11 @@ constexpr int min_blocks() {
   return (std::is_same<TIn, float>::value && std::is_same<TOut, float>::value) ? 4 : 6;
 }
 
-template <typename TIn, typename TOut, bool kVec>
+// THalo: element type of the band-mode halo rows (the input's type, or the output's when the
+// neighbour sent its rows already rounded to it: the rounding commutes with the gather).
+template <typename TIn, typename TOut, typename THalo, bool kVec>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32, min_blocks<TIn, TOut>())
-partition_kernel(const TIn* __restrict__ x, const TIn* __restrict__ halo, TOut* __restrict__ out,
+partition_kernel(const TIn* __restrict__ x, const THalo* __restrict__ halo, TOut* __restrict__ out,
                  LayoutParams p, int64_t B, int32_t D) {
   const int lane = threadIdx.x & 31;
   const int64_t rows = B * (int64_t)p.nW * p.N;
@@ -38,24 +40,32 @@ partition_kernel(const TIn* __restrict__ x, const TIn* __restrict__ halo, TOut* 
     const int32_t n = r - win * p.N;
     const int32_t src = partition_source(p, win, n);
     TOut* dst = out + row * D;
-    // Band mode: sources past the band's own tokens are rows of the halo.
-    const TIn* s = src < tokens ? x + (b * tokens + src) * D
-                                : halo + (b * halo_tokens + (src - tokens)) * D;
+    // Band mode: sources past the band's own tokens are rows of the halo (a warp-uniform branch).
+    const TIn* s = x + (b * tokens + src) * D;
+    const THalo* sh = halo + (b * halo_tokens + (src - tokens)) * D;
     if constexpr (kVec) {
       if (src < 0) {
         for (int c = lane * 8; c < D; c += 256) Vec8<TOut>::zero(dst + c);
-      } else {
+      } else if (src < tokens) {
         for (int c = lane * 8; c < D; c += 256) {
           float v[8];
           Vec8<TIn>::load_stream(s + c, v);
+          Vec8<TOut>::store(dst + c, v);
+        }
+      } else {
+        for (int c = lane * 8; c < D; c += 256) {
+          float v[8];
+          Vec8<THalo>::load_stream(sh + c, v);
           Vec8<TOut>::store(dst + c, v);
         }
       }
     } else {
       if (src < 0) {
         for (int c = lane; c < D; c += 32) dst[c] = from_f32<TOut>(0.f);
-      } else {
+      } else if (src < tokens) {
         for (int c = lane; c < D; c += 32) dst[c] = from_f32<TOut>(to_f32(s[c]));
+      } else {
+        for (int c = lane; c < D; c += 32) dst[c] = from_f32<TOut>(to_f32(sh[c]));
       }
     }
   }
@@ -99,18 +109,18 @@ int64_t grid_for_rows(int64_t rows) {
   return blocks < cap ? (blocks > 0 ? blocks : 1) : cap;
 }
 
-template <typename TIn, typename TOut>
+template <typename TIn, typename TOut, typename THalo = TIn>
 int launch_partition(const void* x, const void* halo, void* out, const LayoutParams& p, int64_t B,
                      int64_t D, cudaStream_t s, bool vec) {
   const int64_t rows = B * (int64_t)p.nW * p.N;
   if (rows == 0 || D == 0) return FA_OK;
   const dim3 grid((unsigned)grid_for_rows(rows)), block(kWarpsPerBlock * 32);
   if (vec)
-    partition_kernel<TIn, TOut, true><<<grid, block, 0, s>>>((const TIn*)x, (const TIn*)halo, (TOut*)out,
-                                                             p, B, (int32_t)D);
+    partition_kernel<TIn, TOut, THalo, true><<<grid, block, 0, s>>>((const TIn*)x, (const THalo*)halo,
+                                                                    (TOut*)out, p, B, (int32_t)D);
   else
-    partition_kernel<TIn, TOut, false><<<grid, block, 0, s>>>((const TIn*)x, (const TIn*)halo, (TOut*)out,
-                                                              p, B, (int32_t)D);
+    partition_kernel<TIn, TOut, THalo, false><<<grid, block, 0, s>>>((const TIn*)x, (const THalo*)halo,
+                                                                     (TOut*)out, p, B, (int32_t)D);
   return check_launch("partition_kernel");
 }
 
@@ -215,7 +225,7 @@ int check_band_args(const void* a, int adt, const void* b, int bdt, int64_t B, i
 
 }  // namespace
 
-extern "C" int fa_roll_pad_partition_band(const void* x, const void* halo, int x_dtype,
+extern "C" int fa_roll_pad_partition_band(const void* x, const void* halo, int x_dtype, int halo_dtype,
                                           void* windows, int windows_dtype, int64_t B, int64_t C,
                                           int64_t H_band, int64_t H_field, int64_t W, int64_t D,
                                           const int32_t window_size[3],
@@ -224,10 +234,18 @@ extern "C" int fa_roll_pad_partition_band(const void* x, const void* halo, int x
   int rc = check_band_args(x, x_dtype, windows, windows_dtype, B, C, H_band, H_field, W, D,
                            window_size, shift_size, &g);
   if (rc != FA_OK) return rc;
+  FA_REQUIRE(halo_dtype == x_dtype || halo_dtype == windows_dtype, FA_ERR_INVALID,
+             "halo_dtype must be x_dtype or windows_dtype");
   const LayoutParams p = band_layout_params(g, false);
   FA_REQUIRE(halo || p.band == 0 || B == 0 || D == 0, FA_ERR_INVALID, "shifted band needs a halo");
   const bool vec = (D % 8 == 0) && aligned16(x) && aligned16(windows) && (!halo || aligned16(halo));
-  return dispatch_partition(x_dtype, windows_dtype, x, halo, windows, p, B, D, (cudaStream_t)stream, vec);
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (halo_dtype == x_dtype) return dispatch_partition(x_dtype, windows_dtype, x, halo, windows, p, B, D, st, vec);
+  // The halo arrives already rounded to the windows' type: only fp32 x -> bf16 windows gains from
+  // that (a bf16 x has nothing to round, its fp32 windows are exact).
+  FA_REQUIRE(x_dtype == FA_F32 && windows_dtype == FA_BF16, FA_ERR_UNSUPPORTED,
+             "a halo in the windows' dtype is supported for fp32 x with bf16 windows");
+  return launch_partition<float, __nv_bfloat16, __nv_bfloat16>(x, halo, windows, p, B, D, st, vec);
 }
 
 extern "C" int fa_band_halo_extract(const void* windows, int windows_dtype, void* halo_out,

@@ -33,9 +33,42 @@ class CapturedStep:
             for _ in range(max(1, warmup)):
                 fn(self.static_input)
         torch.cuda.current_stream(example.device).wait_stream(side)
-        self.graph = torch.cuda.CUDAGraph()
+        # keep_graph: the captured graph stays queryable (kernel_names) after instantiation.
+        self.graph = torch.cuda.CUDAGraph(keep_graph=True)
         with torch.cuda.graph(self.graph):
             self.static_output = fn(self.static_input)
+        self.graph.instantiate()
+
+    def kernel_names(self) -> list[str]:
+        """The (mangled) name of every kernel node of the captured graph: one entry per kernel
+        launch of a replay, this library's and the libraries' (cuBLAS, PyTorch) alike. A name
+        that cannot be resolved is returned as ``"?"``; the count stays exact."""
+        from cuda.bindings import driver as cu
+        from cuda.bindings import runtime as rt
+
+        g = rt.cudaGraph_t(init_value=int(self.graph.raw_cuda_graph()))
+        err, _, n = rt.cudaGraphGetNodes(g, 0)
+        if err != rt.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"cudaGraphGetNodes failed: {err}")
+        err, nodes, n = rt.cudaGraphGetNodes(g, n)
+        if err != rt.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"cudaGraphGetNodes failed: {err}")
+        names = []
+        for node in nodes[:n]:
+            err, kind = rt.cudaGraphNodeGetType(node)
+            if err != rt.cudaError_t.cudaSuccess or kind != rt.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+                continue
+            name = "?"
+            try:
+                err, params = cu.cuGraphKernelNodeGetParams(cu.CUgraphNode(init_value=int(node)))
+                if err == cu.CUresult.CUDA_SUCCESS:
+                    err, raw = cu.cuFuncGetName(params.func)
+                    if err == cu.CUresult.CUDA_SUCCESS and raw:
+                        name = raw.decode() if isinstance(raw, bytes) else str(raw)
+            except Exception:  # noqa: BLE001 - the count does not depend on the name
+                pass
+            names.append(name)
+        return names
 
     def replay(self) -> torch.Tensor:
         """Run the step on the current contents of ``static_input``; returns ``static_output``

@@ -20,11 +20,16 @@ band's region ids are the rows ``[h1_begin, h1_end)`` of the field's ``(nW, N)``
 
 ``exchange`` works for any backend: NCCL tensors on the GPU (the product path) and gloo CPU
 tensors (the multi-process tests). Waits are bounded by ``timeout_s``: a peer that never sends
-surfaces as :class:`HaloExchangeError` on the host, never as a hang.
+surfaces as :class:`HaloExchangeError` on the host, never as a hang. On NCCL the host does not
+block per exchange (the transfers are stream-ordered); each exchange leaves a CUDA event, and
+every later exchange, and :meth:`BandContext.wait`, checks the oldest unfinished one against the
+deadline. On expiry the process group is aborted (which ends NCCL's spinning transfer kernels) and
+:class:`HaloExchangeError` is raised.
 """
 
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass, field
 from datetime import timedelta
 from typing import Callable, Optional
@@ -118,6 +123,8 @@ class BandContext:
         self.next = (self.rank + 1) % self.world
         self._gids: dict = {}
         self._bufs: dict = {}
+        # Unfinished NCCL exchanges: (event after the transfers, host time issued, dst, src).
+        self._pending: list = []
 
     # ------------------------------------------------------------------ geometry
     @property
@@ -186,14 +193,54 @@ class BandContext:
             cuda = recv.is_cuda
             for w in works:
                 if cuda:
-                    w.wait()
+                    w.wait()  # the current stream waits; the host does not
                 else:
                     w.wait(timedelta(seconds=self.timeout_s))
+            if cuda:
+                ev = torch.cuda.Event()
+                ev.record()
+                self._pending.append((ev, time.monotonic(), dst, src))
+                self._check_pending(block=False)
         except HaloExchangeError:
             raise
         except RuntimeError as e:
             raise HaloExchangeError(
                 f"rank {self.rank}: halo exchange (send to {dst}, receive from {src}) failed: {e}") from e
+
+    def _check_pending(self, block: bool) -> None:
+        """Drop finished exchanges; raise when the oldest unfinished one is past the deadline.
+        With ``block`` poll until every pending exchange finished or the deadline passed."""
+        while self._pending:
+            ev, t0, dst, src = self._pending[0]
+            if ev.query():
+                self._pending.pop(0)
+                continue
+            if time.monotonic() - t0 > self.timeout_s:
+                self._pending.clear()
+                self._abort()
+                raise HaloExchangeError(
+                    f"rank {self.rank}: halo exchange (send to {dst}, receive from {src}) did not complete "
+                    f"within {self.timeout_s:.0f} s")
+            if not block:
+                return
+            time.sleep(0.001)
+
+    def _abort(self) -> None:
+        """End the group's communicator so that its transfer kernels stop waiting for the peer."""
+        try:
+            import torch.distributed as dist
+            from torch.distributed import distributed_c10d as c10d
+
+            abort = getattr(c10d, "_abort_process_group", None)
+            if abort is not None and dist.is_initialized():
+                abort(self.group if self.group is not None else dist.group.WORLD)
+        except Exception:  # noqa: BLE001 - the exchange error is what the caller must see
+            pass
+
+    def wait(self) -> None:
+        """Block until every exchange issued so far has completed on the device, or raise
+        :class:`HaloExchangeError` once the oldest of them is ``timeout_s`` old."""
+        self._check_pending(block=True)
 
     def halo_forward(self, x_band: torch.Tensor, s: int, dtype: Optional[torch.dtype] = None) -> torch.Tensor:
         """Receive the next band's first ``s`` rows: ``x_band (B, C, Hb, W, D)`` -> ``(B, C, s, W, D)``.

@@ -242,7 +242,9 @@ class Swin3DTransformerBlock(nn.Module):
                 xw = roll_pad_partition_windows(x5, res, self.window_size, self.shift_size, out_dtype=act)
                 _rec.end("partition", ev, L * D * 4 * B + xw.numel() * e)
             else:
-                halo = band.halo_forward(x5, ss[1]) if ss[1] else None
+                # The halo rows travel already rounded to the windows' dtype (bf16 in bf16_mixed:
+                # half the bytes, bit-identical windows since the rounding commutes with the gather).
+                halo = band.halo_forward(x5, ss[1], dtype=act) if ss[1] else None
                 xw = roll_pad_partition_windows_band(x5, halo, field_res, self.window_size, self.shift_size,
                                                      out_dtype=act)
             T = xw.shape[0] * xw.shape[1]

@@ -131,7 +131,9 @@ def roll_pad_partition_windows_band(
 ) -> torch.Tensor:
     """Windows of one latitude band: ``x (B, C, H_band, W, D)`` + ``halo (B, C, s, W, D)`` (the next
     band's first ``s = shift_h`` rows) -> ``(B * nW_band, N, D)``, equal to rows
-    ``[h1_begin, h1_end)`` of the field's ``roll_pad_partition_windows``."""
+    ``[h1_begin, h1_end)`` of the field's ``roll_pad_partition_windows``. The halo may be in
+    ``x``'s dtype or already in ``out_dtype`` (the neighbour rounded it before sending; the result
+    is the same bit for bit; for fp32 ``x`` and bf16 windows)."""
     if x.device.type != "cuda" or x.dtype not in _DTYPES:
         raise ValueError("roll_pad_partition_windows_band requires CUDA float32/bfloat16 input.")
     out_dtype = x.dtype if out_dtype is None else out_dtype
@@ -139,12 +141,14 @@ def roll_pad_partition_windows_band(
         raise ValueError("out_dtype must be float32 or bfloat16")
     B, C, Hb, W, D = x.shape
     ws, ss, nW, N = band_geometry((C, Hb, W), field_res, window_size, shift_size)
-    halo = _check_halo(halo, B, C, ss[1], W, D, x.dtype, x.device, "halo")
+    pre_rounded = (halo is not None and halo.dtype == out_dtype == torch.bfloat16 and x.dtype == torch.float32)
+    halo_dtype = out_dtype if pre_rounded else x.dtype
+    halo = _check_halo(halo, B, C, ss[1], W, D, halo_dtype, x.device, "halo")
     x = x.contiguous()
     out = torch.empty((B * nW, N, D), device=x.device, dtype=out_dtype)
     rc = _lib.load().fa_roll_pad_partition_band(
         x.data_ptr(), halo.data_ptr() if halo is not None else None, _lib.dtype_code(x.dtype),
-        out.data_ptr(), _lib.dtype_code(out_dtype), B, C, Hb, field_res[1], W, D,
+        _lib.dtype_code(halo_dtype), out.data_ptr(), _lib.dtype_code(out_dtype), B, C, Hb, field_res[1], W, D,
         _lib.i32x3(window_size), _lib.i32x3(shift_size), _lib.stream_ptr(x.device))
     _lib.check(rc, "roll_pad_partition_windows_band")
     return out

@@ -128,6 +128,9 @@ int fa_adaln_film_partition(const void* x, int x_dtype, const void* residual, in
  *
  *  - fa_roll_pad_partition_band: windows of the band; rows past the band are read from `halo`
  *    (B, C, s, W, D), the next band's first s rows (cyclically: the last band takes band 0's).
+ *    halo_dtype is x_dtype, or windows_dtype when the neighbour sends its rows already rounded
+ *    to the windows' type (bit-identical: the rounding commutes with the gather; half the bytes
+ *    for fp32 -> bf16).
  *  - fa_band_halo_extract: halo_out (B, C, s, W, D) = the band's last s shifted rows, unrolled
  *    in C and W; they are the next band's first s original rows (its halo-back buffer).
  *  - fa_crop_roll_unmerge_band / fa_unmerge_adaln_film_band: inverse (plain, or fused with
@@ -138,7 +141,7 @@ int fa_adaln_film_partition(const void* x, int x_dtype, const void* residual, in
  * are the rows [h1_begin, h1_end) of the field's window grid; region ids for a mask are sliced
  * from the field's (nW, N) ids in the same way. With s = 0 the halo pointers may be NULL.
  */
-int fa_roll_pad_partition_band(const void* x, const void* halo, int x_dtype, void* windows,
+int fa_roll_pad_partition_band(const void* x, const void* halo, int x_dtype, int halo_dtype, void* windows,
                                int windows_dtype, int64_t B, int64_t C, int64_t H_band,
                                int64_t H_field, int64_t W, int64_t D, const int32_t window_size[3],
                                const int32_t shift_size[3], void* stream);

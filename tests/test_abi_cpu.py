@@ -95,14 +95,17 @@ def test_band_arguments_return_status_without_a_gpu(lib):
     ws, ss = _lib.i32x3((2, 6, 12)), _lib.i32x3((1, 3, 6))
     p = ctypes.c_void_p(1 << 20)
     # band height not a whole number of window rows
-    rc = lib.fa_roll_pad_partition_band(p, p, 0, p, 0, 1, 4, 9, 36, 72, 64, ws, ss, None)
+    rc = lib.fa_roll_pad_partition_band(p, p, 0, 0, p, 0, 1, 4, 9, 36, 72, 64, ws, ss, None)
     assert rc == _lib.FA_ERR_INVALID and b"band height" in lib.fa_last_error()
     # field height needing padding along H
-    rc = lib.fa_roll_pad_partition_band(p, p, 0, p, 0, 1, 4, 6, 45, 90, 64, ws, ss, None)
+    rc = lib.fa_roll_pad_partition_band(p, p, 0, 0, p, 0, 1, 4, 6, 45, 90, 64, ws, ss, None)
     assert rc == _lib.FA_ERR_UNSUPPORTED and b"multiple of the window height" in lib.fa_last_error()
     # shifted band without its halo
-    rc = lib.fa_roll_pad_partition_band(p, None, 0, p, 0, 1, 4, 12, 36, 72, 64, ws, ss, None)
+    rc = lib.fa_roll_pad_partition_band(p, None, 0, 0, p, 0, 1, 4, 12, 36, 72, 64, ws, ss, None)
     assert rc == _lib.FA_ERR_INVALID and b"halo" in lib.fa_last_error()
+    # a halo in neither the input's nor the windows' dtype
+    rc = lib.fa_roll_pad_partition_band(p, p, 0, 1, p, 0, 1, 4, 12, 36, 72, 64, ws, ss, None)
+    assert rc == _lib.FA_ERR_INVALID and b"halo_dtype" in lib.fa_last_error()
     rc = lib.fa_crop_roll_unmerge_band(p, None, 0, p, 0, 1, 4, 12, 36, 72, 64, ws, ss, None)
     assert rc == _lib.FA_ERR_INVALID and b"halo" in lib.fa_last_error()
     rc = lib.fa_unmerge_adaln_film_band(p, None, 0, p, 0, p, p, 0, 0.0, 1e-5, p, 0, None,

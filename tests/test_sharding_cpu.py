@@ -189,3 +189,34 @@ def test_gloo_silent_peer_times_out():
     assert kind == "timeout", out
     elapsed, msg = val
     assert elapsed < 15 and "rank 0" in msg
+
+
+def test_nccl_exchange_deadline_bookkeeping(monkeypatch):
+    """The stream-ordered (NCCL) exchanges leave events that later exchanges and ``wait`` check:
+    finished ones are dropped, and the oldest unfinished one past ``timeout_s`` raises
+    HaloExchangeError after aborting the group (faked here: no GPU and no process group)."""
+    import time
+
+    from flash_aurora_b200.sharding import BandContext, HaloExchangeError
+
+    class Ev:
+        def __init__(self, done):
+            self.done = done
+
+        def query(self):
+            return self.done
+
+    ctx = BandContext((4, 36, 72), (2, 6, 12), 0, 2, timeout_s=5.0)
+    aborted = []
+    monkeypatch.setattr(ctx, "_abort", lambda: aborted.append(True))
+    now = time.monotonic()
+    ctx._pending = [(Ev(True), now - 100, 1, 1), (Ev(False), now, 1, 1)]
+    ctx._check_pending(block=False)  # the finished one goes, the young unfinished one stays
+    assert len(ctx._pending) == 1 and not aborted
+    ctx._pending = [(Ev(False), now - 10, 1, 1)]
+    with pytest.raises(HaloExchangeError, match="did not complete"):
+        ctx.wait()
+    assert aborted and ctx._pending == []
+    ctx._pending = [(Ev(True), now, 1, 1)]
+    ctx.wait()
+    assert ctx._pending == []
