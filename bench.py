@@ -232,11 +232,11 @@ def run_reference(args) -> None:
 # Operators of the block forward as the step recorder names them: (bound, implementation).
 OPERATORS = {
     "partition": ("hbm", "this library: partition_kernel (first block of each stage)"),
-    "qkv_gemm": ("tensor", "cuBLAS bf16 GEMM"),
+    "qkv_gemm": ("tensor", "this library: tcgen05 GEMM, bias epilogue (CTA pair, 256 x 256 tiles)"),
     "attention": ("hbm", "this library: attn_tc_bf16_kernel (tcgen05)"),
-    "proj_gemm": ("tensor", "cuBLAS bf16 GEMM"),
+    "proj_gemm": ("tensor", "this library: tcgen05 GEMM, bias epilogue (CTA pair, 256 x 256 tiles)"),
     "adaln1_unmerge": ("hbm", "this library: adaln_kernel (unmerge-fused, bf16 copy)"),
-    "fc1_gelu_gemm": ("tensor", "this library: gemm_bias_act_kernel<gelu> (tcgen05)"),
+    "fc1_gelu_gemm": ("tensor", "this library: tcgen05 GEMM + GELU epilogue (single CTA at K=512, CTA pair above)"),
     "fc2_gemm": ("tensor", "cuBLAS bf16 GEMM"),
     "adaln2_partition": ("hbm", "this library: adaln_kernel (next-partition fused)"),
     "adaln2": ("hbm", "this library: adaln_kernel"),
@@ -743,6 +743,43 @@ def run_layout_adaln(args) -> None:
         del a, w, b
 
 
+def run_gemm(args) -> None:
+    """Every bf16 GEMM of the config-4 block at each stage (qkv, proj, fc1 + GELU, fc2): this
+    library's single-CTA and CTA-pair tcgen05 kernels against cuBLAS (``F.linear``, + GELU for
+    fc1), CUDA events, L2 flushed, TFLOP/s against the measured burst bf16 peak."""
+    import flash_aurora_b200 as fa
+    dev = torch.device("cuda", 0)
+    _, tf_peak, kind = _peaks()
+    flush = L2Flush(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    shapes = []
+    for tag, T, L, D in (("S1", 259200, 259200, 512), ("S2", 64800, 64800, 1024), ("S3", 18432, 16200, 2048)):
+        shapes += [(tag, "qkv", T, D, 3 * D, "none"), (tag, "proj", T, D, D, "none"),
+                   (tag, "fc1", L, D, 4 * D, "gelu"), (tag, "fc2", L, 4 * D, D, "none")]
+    for tag, name, M, K, N, act in shapes:
+        a = torch.randn(M, K, device=dev, generator=g).bfloat16()
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()
+        b = (torch.randn(N, device=dev, generator=g) * 0.02).bfloat16()
+        flops = 2 * M * N * K
+        res = {}
+        for kernel in ("single", "pair"):
+            os.environ["FA_GEMM_KERNEL"] = kernel
+            res[kernel] = _time_launches(lambda: fa.linear_bias_act(a, w, b, act=act), args.steps, flush=flush)
+        os.environ.pop("FA_GEMM_KERNEL", None)
+        if act == "gelu":
+            res["cublas"] = _time_launches(lambda: fa.gelu_erf(torch.nn.functional.linear(a, w, b), inplace=True),
+                                           args.steps, flush=flush)
+        else:
+            res["cublas"] = _time_launches(lambda: torch.nn.functional.linear(a, w, b), args.steps, flush=flush)
+        print(json.dumps({"workload": f"config4 {tag} {name} (M={M}, K={K}, N={N}, act={act})",
+                          **{f"{k}_ms": round(v, 4) for k, v in res.items()},
+                          **{f"{k}_tflops": round(flops / (v * 1e-3) / 1e12, 1) for k, v in res.items()},
+                          "peak": tf_peak, "peak_kind": kind}), flush=True)
+        del a, w, b
+    from flash_aurora_b200.status import check_device_status
+    check_device_status(dev)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -752,7 +789,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sharded", action="store_true", help="skip the config-5 sharded-stage object")
     ap.add_argument("--no-bars", action="store_true", help="skip the same-box stock PyTorch comparison")
-    ap.add_argument("--workload", choices=["backbone", "attention", "layout_adaln", "adaln_stages", "sharded"], default="backbone")
+    ap.add_argument("--workload", choices=["backbone", "attention", "layout_adaln", "adaln_stages", "sharded", "gemm"],
+                    default="backbone")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -762,6 +800,8 @@ def main() -> None:
         return run_layout_adaln(args)
     if args.workload == "adaln_stages":
         return run_adaln_stages(args)
+    if args.workload == "gemm":
+        return run_gemm(args)
     if args.workload == "sharded" and args.impl != "reference":
         return run_sharded(args)
     if args.impl == "reference":

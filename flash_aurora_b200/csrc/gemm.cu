@@ -23,6 +23,8 @@
 // (fa_gemm_status), sets an abort flag, frees TMEM and returns.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -61,6 +63,55 @@ struct Params {
   int64_t ldo;  // output row stride in elements
   int* status;
 };
+
+// Epilogue of one warp: the 32 rows of its TMEM lane quarter (starting at global row `row0`) and
+// 128 accumulator columns starting at TMEM address `ta` (global column `col0`): + bias, optional
+// GELU (fitted erfc form on the fp32 sum), one bf16 rounding, staged as 32 x 64 blocks (128-byte
+// swizzle) and written with bulk tensor stores, which drop rows past M.
+template <bool kGelu>
+__device__ __forceinline__ void store_tile_half(uint32_t ta, int col0, int row0, uint32_t stage,
+                                                const __nv_bfloat16* __restrict__ bias, const CUtensorMap* tmo,
+                                                int lane) {
+#pragma unroll 1
+  for (int c = 0; c < 128; c += 64) {
+    uint32_t r0[32], r1[32];
+    tmem_ld32(ta + (uint32_t)c, r0);
+    tmem_ld32(ta + (uint32_t)c + 32, r1);
+    tmem_wait_ld();
+    const int col = col0 + c;
+    // bias: the same 64 values for every lane of the warp (broadcast loads)
+    const uint4* bp = reinterpret_cast<const uint4*>(bias + col);
+    uint32_t pk[32];
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      const uint4 bw = __ldg(bp + v);
+      const uint32_t bb[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int idx = 8 * v + 2 * e;  // column pair within the 64
+        const uint32_t* src = idx < 32 ? r0 : r1;
+        const int si = idx & 31;
+        const float2 bf = unpack_bf16x2(bb[e]);
+        float2 y = make_float2(__uint_as_float(src[si]) + bf.x, __uint_as_float(src[si + 1]) + bf.y);
+        if constexpr (kGelu) y = gelu2_poly(y);
+        pk[4 * v + e] = pack_bf16x2(y.x, y.y);
+      }
+    }
+    // The previous copy must have read the staging tile first.
+    if (lane == 0) bulk_wait_group_read0();
+    __syncwarp();
+    const uint32_t srow = stage + (uint32_t)lane * 128u;
+#pragma unroll
+    for (int v = 0; v < 8; ++v)
+      st_shared_v4(srow + (uint32_t)((v ^ (lane & 7)) << 4), pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+    fence_proxy_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmo, stage, col, row0);
+      bulk_commit_group();
+    }
+  }
+}
 
 template <bool kGelu>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -171,48 +222,8 @@ gemm_bias_act_kernel(const __grid_constant__ CUtensorMap tma, const __grid_const
       const int m0 = (t / p.tiles_n) * kBM, n0 = (t % p.tiles_n) * kBN;
       if (!mbar_wait(BAR(kAccFull + buf), (uint32_t)((j >> 1) & 1), abort, p.status, 6, kTimeoutNs)) break;
       tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < 128; c += 64) {
-        uint32_t r0[32], r1[32];
-        const uint32_t ta = tmem + lane_addr + (uint32_t)buf * kBN + (uint32_t)(half * 128 + c);
-        tmem_ld32(ta, r0);
-        tmem_ld32(ta + 32, r1);
-        tmem_wait_ld();
-        const int col = n0 + half * 128 + c;
-        // bias: the same 64 values for every lane of the warp (broadcast loads)
-        const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col);
-        uint32_t pk[32];
-#pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          const uint4 bw = __ldg(bp + v);
-          const uint32_t bb[4] = {bw.x, bw.y, bw.z, bw.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int idx = 8 * v + 2 * e;  // column pair within the 64
-            const uint32_t* src = idx < 32 ? r0 : r1;
-            const int si = idx & 31;
-            const float2 bf = unpack_bf16x2(bb[e]);
-            float2 y = make_float2(__uint_as_float(src[si]) + bf.x, __uint_as_float(src[si + 1]) + bf.y);
-            if constexpr (kGelu) y = gelu2_poly(y);
-            pk[4 * v + e] = pack_bf16x2(y.x, y.y);
-          }
-        }
-        // Stage the warp's 32 x 64 block (row = lane, 128-byte swizzle) and store it with one
-        // bulk tensor copy; the copy drops rows past M. The previous copy must have read the
-        // staging tile first.
-        if (lane == 0) bulk_wait_group_read0();
-        __syncwarp();
-        const uint32_t srow = stage + (uint32_t)lane * 128u;
-#pragma unroll
-        for (int v = 0; v < 8; ++v)
-          st_shared_v4(srow + (uint32_t)((v ^ (lane & 7)) << 4), pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmo, stage, col, m0 + q * 32);
-          bulk_commit_group();
-        }
-      }
+      store_tile_half<kGelu>(tmem + lane_addr + (uint32_t)buf * kBN + (uint32_t)(half * 128), n0 + half * 128,
+                             m0 + q * 32, stage, p.bias, &tmo, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(kAccEmpty + buf));
@@ -225,6 +236,173 @@ gemm_bias_act_kernel(const __grid_constant__ CUtensorMap tma, const __grid_const
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+
+// ------------------------------------------------------------------------------------------------
+// CTA-pair variant (cluster of 2, tcgen05 cta_group::2): 256 x 256 output tiles per pair.
+//
+// The even CTA of the pair issues one UMMA of M = 256, N = 256, K = 16 that reads A rows 0..127
+// and W rows 0..127 from the even CTA's shared memory and A rows 128..255 / W rows 128..255 from
+// the odd CTA's, and accumulates each CTA's 128 rows x 256 columns in its own TMEM. Per CTA a
+// K slice brings 32 KB (A half + W half) for the same 128 x 256 x 64 products that cost the
+// single-CTA kernel 48 KB: two thirds of the shared-memory fill per FLOP.
+//   warp 0 (both CTAs)   TMA producer of its own halves; the bytes of both CTAs are counted on the
+//                        even CTA's `full` barrier (cta_group::2 form of the tile load, no multicast).
+//   warp 1 (both CTAs)   allocates 512 TMEM columns with cta_group::2; in the even CTA one thread
+//                        issues the UMMAs and commits to the `empty` / `acc_full` barriers of both
+//                        CTAs (tcgen05.commit with a CTA mask).
+//   warps 2-9 (both)     epilogue of the CTA's 128 rows (store_tile_half); each warp releases the
+//                        accumulator by arriving on the even CTA's `acc_empty` barrier.
+// Every wait is bounded as in the single-CTA kernel; both CTAs meet at cluster barriers after set-up
+// (before any remote arrive) and before the TMEM is freed (after every remote access).
+// ------------------------------------------------------------------------------------------------
+constexpr int kPairStages = 6;
+constexpr int kPairHalfBytes = 128 * kBK * 2;            // 16 KB: A half or W half of a K slice
+constexpr int kPairStageBytes = 2 * kPairHalfBytes;      // 32 KB per CTA and stage
+constexpr int kPairNumBars = 2 * kPairStages + 5;
+constexpr int kPairSmem = kPairStages * kPairStageBytes + kEpiWarps * kStageOutBytes + kPairNumBars * 8 + 16 + 1024;
+static_assert(kPairSmem <= 227 * 1024, "shared memory budget (pair)");
+constexpr uint32_t kPairIdesc = make_idesc(1, 256, kBN, false, false);
+enum { kPFull = 0, kPEmpty = kPairStages, kPAccFull = 2 * kPairStages, kPAccEmpty = kPAccFull + 2,
+       kPDone = kPAccEmpty + 2 };
+
+template <bool kGelu>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+gemm_pair_bias_act_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmw,
+                          const __grid_constant__ CUtensorMap tmo, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t sout = sbase + kPairStages * kPairStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPairStages * kPairStageBytes + kEpiWarps * kStageOutBytes);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kPairNumBars);
+  const uint32_t bar0 = smem_u32(bars);
+  auto BAR = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
+  __shared__ int abort_flag;
+  volatile int* abort = &abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: issues the UMMAs; 1: its partner
+  const int pair = (int)blockIdx.x >> 1, npairs = (int)gridDim.x >> 1;
+  const int n_local = p.num_tiles > pair ? (p.num_tiles - 1 - pair) / npairs + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(BAR(kPFull + s), 1);
+      mbar_init(BAR(kPEmpty + s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(BAR(kPAccFull + b), 1);
+      mbar_init(BAR(kPAccEmpty + b), 2 * kEpiWarps);
+    }
+    mbar_init(BAR(kPDone), 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_holder), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the partner's barriers exist before any remote arrive or complete_tx
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tma);
+      tma_prefetch_desc(&tmw);
+      int it = 0;
+      int last_par[kPairStages];
+      for (int s = 0; s < kPairStages; ++s) last_par[s] = -1;
+      bool ok = true;
+      for (int j = 0; j < n_local && ok; ++j) {
+        const int t = pair + j * npairs;
+        const int m0 = (t / p.tiles_n) * 256 + (int)rank * 128, n0 = (t % p.tiles_n) * kBN + (int)rank * 128;
+        for (int kb = 0; kb < p.k_iters; ++kb, ++it) {
+          const int s = it % kPairStages;
+          const uint32_t ph = (uint32_t)((it / kPairStages) & 1);
+          if (!mbar_wait(BAR(kPEmpty + s), ph ^ 1u, abort, p.status, 7, kTimeoutNs)) { ok = false; break; }
+          const uint32_t sa = sbase + s * kPairStageBytes;
+          const uint32_t full0 = map_shared_rank(BAR(kPFull + s), 0);
+          if (rank == 0) mbar_arrive_expect_tx(BAR(kPFull + s), (uint32_t)(2 * kPairStageBytes));
+          tma_load_2d_pair(sa, &tma, full0, kb * kBK, m0);
+          tma_load_2d_pair(sa + kPairHalfBytes, &tmw, full0, kb * kBK, n0);
+          last_par[s] = (int)ph;
+        }
+      }
+      // Never leave with bulk copies in flight: the even CTA's `full` barriers count both CTAs'
+      // bytes, so it waits for them (bounded); the odd CTA is held by the final cluster barrier.
+      if (rank == 0) {
+        int no_abort = 0;
+        for (int s = 0; s < kPairStages; ++s)
+          if (last_par[s] >= 0)
+            mbar_wait(BAR(kPFull + s), (uint32_t)last_par[s], &no_abort, p.status, 8, kTimeoutNs);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int j = 0; j < n_local && ok; ++j) {
+        const int buf = j & 1;
+        if (!mbar_wait(BAR(kPAccEmpty + buf), (uint32_t)(((j >> 1) & 1) ^ 1), abort, p.status, 9, kTimeoutNs)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)buf * kBN;
+        for (int kb = 0; kb < p.k_iters; ++kb, ++it) {
+          const int s = it % kPairStages;
+          if (!mbar_wait(BAR(kPFull + s), (uint32_t)((it / kPairStages) & 1), abort, p.status, 10, kTimeoutNs)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = sbase + s * kPairStageBytes, sw = sa + kPairHalfBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16_pair(d, desc_sw128(sa + kk * 32, 16, 1024), desc_sw128(sw + kk * 32, 16, 1024), kPairIdesc,
+                          (kb | kk) ? 1u : 0u);
+          umma_commit_pair(BAR(kPEmpty + s), 0x3);
+        }
+        if (ok) umma_commit_pair(BAR(kPAccFull + buf), 0x3);
+      }
+      umma_commit_pair(BAR(kPDone), 0x1);
+      int no_abort = 0;
+      mbar_wait(BAR(kPDone), 0, &no_abort, p.status, 11, kTimeoutNs);
+    }
+  } else {
+    // ---------------- epilogue (both CTAs: this CTA's 128 rows of the pair's tile) ----------------
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    const uint32_t stage = sout + (uint32_t)(warp - 2) * kStageOutBytes;
+    if (lane == 0) tma_prefetch_desc(&tmo);
+    for (int j = 0; j < n_local; ++j) {
+      const int buf = j & 1;
+      const int t = pair + j * npairs;
+      const int m0 = (t / p.tiles_n) * 256 + (int)rank * 128, n0 = (t % p.tiles_n) * kBN;
+      if (!mbar_wait(BAR(kPAccFull + buf), (uint32_t)((j >> 1) & 1), abort, p.status, 12, kTimeoutNs)) break;
+      tc_fence_after();
+      store_tile_half<kGelu>(tmem + lane_addr + (uint32_t)buf * kBN + (uint32_t)(half * 128), n0 + half * 128,
+                             m0 + q * 32, stage, p.bias, &tmo, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(BAR(kPAccEmpty + buf));
+        else mbar_arrive_remote(map_shared_rank(BAR(kPAccEmpty + buf), 0));
+      }
+    }
+    if (lane == 0) bulk_wait_group0();
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no remote access to the partner's shared memory or TMEM after this point
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
   }
 }
 
@@ -272,6 +450,15 @@ int make_out_map(CUtensorMap* map, void* base, int64_t M, int64_t N, int64_t ld)
   return FA_OK;
 }
 
+// 0: choose by shape; 1: single-CTA kernel; 2: CTA-pair kernel (FA_GEMM_KERNEL=single|pair).
+int kernel_choice() {
+  const char* e = getenv("FA_GEMM_KERNEL");
+  if (!e) return 0;
+  if (!strcmp(e, "single")) return 1;
+  if (!strcmp(e, "pair")) return 2;
+  return 0;
+}
+
 int* status_ptr() {
   int* ptr = nullptr;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_status) != cudaSuccess) return nullptr;
@@ -298,15 +485,22 @@ extern "C" int fa_linear_bias_act(const void* a, const void* w, const void* bias
              "a, w, bias and out must be 16-byte aligned");
   FA_REQUIRE(lda >= K && ldw >= K && ldo >= N && lda % 8 == 0 && ldw % 8 == 0 && ldo % 8 == 0, FA_ERR_INVALID,
              "row strides must cover the rows and be multiples of 8 elements");
+  // Kernel: the CTA-pair kernel (256 x 256 tiles, two thirds of the shared-memory fill per FLOP)
+  // except for the GELU epilogue at K < 1024, where the epilogue sets the tile period and the
+  // pair's coupled tiles measured slower (config-4 stage 1 fc1: 0.59 against 0.55 ms);
+  // FA_GEMM_KERNEL=single|pair forces one (tests).
+  const int choice = gemm::kernel_choice();
+  const bool use_pair = choice == 2 || (choice == 0 && !(act == FA_ACT_GELU && K < 1024));
+  const int64_t tile_m = use_pair ? 256 : gemm::kBM;
   CUtensorMap ma, mw, mo;
   int rc;
   if ((rc = gemm::make_map(&ma, a, M, K, lda, gemm::kBM)) != FA_OK) return rc;
-  if ((rc = gemm::make_map(&mw, w, N, K, ldw, gemm::kBN)) != FA_OK) return rc;
+  if ((rc = gemm::make_map(&mw, w, N, K, ldw, use_pair ? 128u : (uint32_t)gemm::kBN)) != FA_OK) return rc;
   if ((rc = gemm::make_out_map(&mo, out, M, N, ldo)) != FA_OK) return rc;
   gemm::Params p{};
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
   p.tiles_n = (int)(N / gemm::kBN);
-  const int64_t tiles = ((M + gemm::kBM - 1) / gemm::kBM) * p.tiles_n;
+  const int64_t tiles = ((M + tile_m - 1) / tile_m) * p.tiles_n;
   FA_REQUIRE(tiles < ((int64_t)1 << 31), FA_ERR_INVALID, "too many tiles");
   p.num_tiles = (int)tiles;
   p.k_iters = (int)(K / gemm::kBK);
@@ -315,6 +509,14 @@ extern "C" int fa_linear_bias_act(const void* a, const void* w, const void* bias
   p.ldo = ldo;
   p.status = gemm::status_ptr();
   FA_REQUIRE(p.status, FA_ERR_CUDA, "cannot resolve the GEMM status word");
+  if (use_pair) {
+    auto kern = act == FA_ACT_GELU ? gemm::gemm_pair_bias_act_kernel<true> : gemm::gemm_pair_bias_act_kernel<false>;
+    FA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kPairSmem));
+    const int pairs_max = num_sms() / 2;
+    const int pairs = p.num_tiles < pairs_max ? p.num_tiles : pairs_max;
+    kern<<<2 * pairs, gemm::kThreads, gemm::kPairSmem, (cudaStream_t)stream>>>(ma, mw, mo, p);
+    return check_launch("gemm_pair_bias_act_kernel");
+  }
   auto kern = act == FA_ACT_GELU ? gemm::gemm_bias_act_kernel<true> : gemm::gemm_bias_act_kernel<false>;
   FA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kSmem));
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();

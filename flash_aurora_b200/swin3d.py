@@ -9,10 +9,10 @@ path (the upstream pure-PyTorch path is the test oracle, not part of this packag
 Per block (upstream swin3d.py:706-815, post-norm), precision ``"bf16_mixed"``:
 
 1. ``fa_roll_pad_partition``: fp32 residual -> bf16 windows (shift + pad + partition + cast).
-2. QKV linear, bf16 in/out (cuBLAS).
+2. QKV linear, bf16 in/out (``fa_linear_bias_act``: tcgen05 GEMM, bias epilogue).
 3. ``fa_window_attention_qkvpacked``: bf16 window attention reading the packed QKV, shifted
    blocks masked by region ids, output in the (window, token, channel) layout.
-4. proj linear, bf16 (cuBLAS).
+4. proj linear, bf16 (``fa_linear_bias_act``).
 5. ``fa_unmerge_adaln_film``: crop/un-roll/merge of the proj output fused into
    ``x1 = x + AdaLN1(.)`` (fp32), plus a bf16 copy of ``x1`` for fc1.
 6. ``fa_linear_bias_act``: fc1 + bias + exact GELU in one tcgen05 kernel (bf16 out) -> fc2 (bf16,
@@ -176,6 +176,15 @@ class Swin3DTransformerBlock(nn.Module):
         self.mlp = MLP(dim, int(dim * mlp_ratio))
         self._bf16 = _CastCache()
 
+    @staticmethod
+    def _linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], bf16: bool) -> torch.Tensor:
+        """The block's bf16 linears on this library's tcgen05 GEMM where its tile shape fits (out
+        features a multiple of 256, in features a multiple of 64, a bias), else cuBLAS; FP32 tiers
+        always use cuBLAS (strict FP32 or TF32)."""
+        if bf16 and b is not None and w.shape[0] % 256 == 0 and w.shape[1] % 64 == 0:
+            return linear_bias_act(x, w, b, act="none")
+        return F.linear(x, w, b)
+
     def _w(self, lin: nn.Linear, bf16: bool):
         if not bf16:
             return lin.weight, lin.bias
@@ -250,7 +259,7 @@ class Swin3DTransformerBlock(nn.Module):
             T = xw.shape[0] * xw.shape[1]
             wq, bq = self._w(self.attn.qkv, bf16)
             ev = _rec.begin()
-            qkv = F.linear(xw, wq, bq)
+            qkv = self._linear(xw, wq, bq, bf16)
             _rec.end("qkv_gemm", ev, (T * D + 3 * D * D + 3 * T * D) * e, 2 * T * D * 3 * D)
             ev = _rec.begin()
             a = window_attn_fwd_cute_qkvpacked(qkv, heads, group_ids=gids, output_layout="bnc")
@@ -258,7 +267,7 @@ class Swin3DTransformerBlock(nn.Module):
             _rec.end("attention", ev, 4 * T * D * e, 4 * xw.shape[0] * heads * Nw * Nw * (D // heads))
             wp, bp = self._w(self.attn.proj, bf16)
             ev = _rec.begin()
-            a = F.linear(a, wp, bp)
+            a = self._linear(a, wp, bp, bf16)
             _rec.end("proj_gemm", ev, (2 * T * D + D * D) * e, 2 * T * D * D)
             x1_bf16 = torch.empty(B, L, D, device=x.device, dtype=torch.bfloat16) if bf16 else None
             ev = _rec.begin()

@@ -4,11 +4,14 @@ Parameters are plain dicts keyed exactly like the upstream ``state_dict`` (for e
 ``"attn.qkv.weight"``, ``"norm1.ln_modulation.1.bias"``), so a state dict of the upstream
 modules, or of the product modules in ``flash_aurora_b200.swin3d``, feeds this oracle directly.
 
-``bf16_mixed=True`` rounds to bfloat16 at exactly the points where the upstream ``bf16_mixed``
-tier does (BF16 autocast around the attention and MLP linears, BF16 window attention,
-custom_op_paths.py:188-263, swin3d.py:291-407, swin3d.py:73-109); everything else stays FP32.
-That gives a tight reference for the BF16 GPU path. With ``bf16_mixed=False`` every step is
-strict FP32, the reference for the FP32/3xTF32 tier.
+``bf16_mixed=True`` rounds where the upstream ``bf16_mixed`` tier rounds on its GPU path: bfloat16
+around the attention and MLP linears (autocast, custom_op_paths.py:188-263, swin3d.py:291-407,
+swin3d.py:73-109), bfloat16 probabilities in the window attention's P.V product
+(ops/cute/_kernel_bf16.py:418-424), and TF32 operands in the other FP32 linears (time embedding,
+AdaLN modulation, patch merge/split: ``_hybrid_linear``); everything else stays FP32. That is
+the emulated upstream tier: its drift from the FP32 oracle is the reference's own tier drift, and
+it is a tight reference for the BF16 GPU path. With ``bf16_mixed=False`` every step is strict
+FP32, the reference for the FP32/3xTF32 tier.
 
 Upstream semantics restated (paths relative to the Flash-Aurora project):
 
@@ -34,6 +37,22 @@ import torch.nn.functional as F
 from . import layout as L
 
 
+def _tf32(t: torch.Tensor, on: bool) -> torch.Tensor:
+    """Round FP32 to TF32 (10 mantissa bits, to nearest, ties away from zero), when ``on``: the
+    operand rounding of a TF32 tensor-core GEMM."""
+    if not on:
+        return t
+    i = t.float().contiguous().view(torch.int32)
+    return ((i + 0x1000) & ~0x1FFF).view(torch.float32)
+
+
+def tf32_linear(x, w, b=None, *, tf32: bool = False):
+    """``F.linear`` with TF32 operands (FP32 accumulation) when ``tf32``: upstream's bf16_mixed
+    tier runs every FP32 backbone linear outside attention and the MLP (time embedding, AdaLN
+    modulation, patch merge/split) as a TF32 GEMM (custom_op_paths.py:188-263, ``_hybrid_linear``)."""
+    return F.linear(_tf32(x, tf32), _tf32(w, tf32), b)
+
+
 def _bf(t: torch.Tensor, on: bool) -> torch.Tensor:
     """Round to bfloat16 and back (round-to-nearest-even), when ``on``."""
     return t.to(torch.bfloat16).to(torch.float32) if on else t
@@ -49,9 +68,9 @@ def linear(x, w, b=None, *, bf16: bool = False):
     return _bf(y, bf16)
 
 
-def adaln_modulation(c, p, prefix):
+def adaln_modulation(c, p, prefix, *, tf32: bool = False):
     """film.py:82,117: ``shift, scale = Linear(SiLU(c)).unsqueeze(1).chunk(2)`` (shift first)."""
-    mod = F.linear(F.silu(c), p[prefix + "ln_modulation.1.weight"], p[prefix + "ln_modulation.1.bias"])
+    mod = tf32_linear(F.silu(c), p[prefix + "ln_modulation.1.weight"], p[prefix + "ln_modulation.1.bias"], tf32=tf32)
     shift, scale = mod.unsqueeze(1).chunk(2, dim=-1)
     return shift, scale
 
@@ -78,13 +97,35 @@ def window_attention_core(q, k, v, mask=None, scale=None):
     return torch.einsum("bhnm,bhmd->bhnd", torch.softmax(s, dim=-1), v)
 
 
-def window_attention(xw, mask, p, prefix, num_heads, *, bf16: bool = False):
-    """swin3d.py:253-409 for one block: qkv -> attention -> proj (FP32 result)."""
+def window_attention_core_bf16p(q, k, v, mask=None, scale=None):
+    """The upstream bf16 window-attention kernel's rounding (ops/cute/_kernel_bf16.py:418-424,
+    501-503): the unnormalised probabilities ``exp(s - rowmax)`` are rounded to bfloat16 before the
+    P.V product, which accumulates in FP32; the row sum and the final division stay FP32."""
+    Bwin, H, N, Dh = q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(Dh)
+    s = torch.einsum("bhnd,bhmd->bhnm", q, k) * scale
+    if mask is not None:
+        idx = torch.arange(Bwin) % mask.shape[0]
+        s = s + mask[idx].unsqueeze(1)
+    pr = torch.exp(s - s.amax(dim=-1, keepdim=True))
+    return torch.einsum("bhnm,bhmd->bhnd", _bf(pr, True), v) / pr.sum(dim=-1, keepdim=True)
+
+
+def window_attention(xw, mask, p, prefix, num_heads, *, bf16: bool = False, chunk: int = 256):
+    """swin3d.py:253-409 for one block: qkv -> attention -> proj (FP32 result). With ``bf16`` the
+    attention follows the upstream bf16 kernel's rounding (:func:`window_attention_core_bf16p`).
+    Windows are processed ``chunk`` at a time to bound the memory of the logits."""
     Bwin, N, D = xw.shape
     Dh = D // num_heads
     qkv = linear(xw, p[prefix + "qkv.weight"], p[prefix + "qkv.bias"], bf16=bf16)
     qkv = qkv.view(Bwin, N, 3, num_heads, Dh).permute(2, 0, 3, 1, 4)
-    o = window_attention_core(qkv[0], qkv[1], qkv[2], mask)
+    core = window_attention_core_bf16p if bf16 else window_attention_core
+    if mask is None or mask.shape[0] == Bwin:
+        o = torch.cat([core(qkv[0][i:i + chunk], qkv[1][i:i + chunk], qkv[2][i:i + chunk],
+                            None if mask is None else mask[i:i + chunk]) for i in range(0, Bwin, chunk)])
+    else:
+        o = core(qkv[0], qkv[1], qkv[2], mask)
     o = _bf(o, bf16).permute(0, 2, 1, 3).reshape(Bwin, N, D)
     return linear(o, p[prefix + "proj.weight"], p[prefix + "proj.bias"], bf16=bf16)
 
@@ -112,14 +153,14 @@ def block_forward(x, c, res, p, *, num_heads, window_size, shift_size, prefix=""
     xw = torch.from_numpy(L.roll_pad_partition(x.view(B, C, H, W, D).numpy(), res, window_size, shift_size))
     aw = window_attention(xw, mask, p, prefix + "attn.", num_heads, bf16=bf16_mixed)
     a = torch.from_numpy(L.crop_roll_unmerge(aw.numpy(), res, window_size, shift_size)).reshape(B, Ltok, D)
-    sh1, sc1 = adaln_modulation(c, p, prefix + "norm1.")
+    sh1, sc1 = adaln_modulation(c, p, prefix + "norm1.", tf32=bf16_mixed)
     x = x + adaln(a, sh1, sc1, eps=eps)
     h = mlp(x, p, prefix + "mlp.", bf16=bf16_mixed)
-    sh2, sc2 = adaln_modulation(c, p, prefix + "norm2.")
+    sh2, sc2 = adaln_modulation(c, p, prefix + "norm2.", tf32=bf16_mixed)
     return x + adaln(h, sh2, sc2, eps=eps)
 
 
-def patch_merge(x, res, p, prefix):
+def patch_merge(x, res, p, prefix, *, tf32: bool = False):
     """swin3d.py:830-861: pad H/W to even, gather 2x2 -> 4D, LayerNorm(4D), Linear(4D->2D)."""
     C, H, W = res
     B, _, D = x.shape
@@ -129,14 +170,14 @@ def patch_merge(x, res, p, prefix):
     x = x.reshape(B, C, nH // 2, 2, nW_ // 2, 2, D).permute(0, 1, 2, 4, 3, 5, 6)
     x = x.reshape(B, C * (nH // 2) * (nW_ // 2), 4 * D)
     x = F.layer_norm(x, (4 * D,), p[prefix + "norm.weight"], p[prefix + "norm.bias"])
-    return F.linear(x, p[prefix + "reduction.weight"])
+    return tf32_linear(x, p[prefix + "reduction.weight"], tf32=tf32)
 
 
-def patch_split(x, res, crop, p, prefix):
+def patch_split(x, res, crop, p, prefix, *, tf32: bool = False):
     """swin3d.py:879-919: Linear(D->2D), 2x2 -> spatial, crop, LayerNorm(D/2), Linear."""
     C, H, W = res
     B, _, D = x.shape
-    x = F.linear(x, p[prefix + "lin1.weight"])
+    x = tf32_linear(x, p[prefix + "lin1.weight"], tf32=tf32)
     D2 = x.shape[-1]
     x = x.view(B, C, H, W, 2, 2, D2 // 4).permute(0, 1, 2, 4, 3, 5, 6)
     x = x.reshape(B, C, 2 * H, 2 * W, D2 // 4)
@@ -144,7 +185,7 @@ def patch_split(x, res, crop, p, prefix):
     x = x[:, : x.shape[1] - cC, : x.shape[2] - cH, : x.shape[3] - cW, :]
     x = x.reshape(B, -1, D2 // 4)
     x = F.layer_norm(x, (D2 // 4,), p[prefix + "norm.weight"], p[prefix + "norm.bias"])
-    return F.linear(x, p[prefix + "lin2.weight"])
+    return tf32_linear(x, p[prefix + "lin2.weight"], tf32=tf32)
 
 
 def lead_time_expansion(hours: torch.Tensor, d: int) -> torch.Tensor:
@@ -184,8 +225,9 @@ def backbone_forward(x, lead_time: timedelta, patch_res, p, *, embed_dim, encode
     hours = lead_time / timedelta(hours=1)
     lt = torch.full((x.shape[0],), hours, dtype=torch.float32)
     e = lead_time_expansion(lt, embed_dim)
-    c = F.linear(F.silu(F.linear(e, p["time_mlp.0.weight"], p["time_mlp.0.bias"])),
-                 p["time_mlp.2.weight"], p["time_mlp.2.bias"])
+    t32 = bf16_mixed
+    c = tf32_linear(F.silu(tf32_linear(e, p["time_mlp.0.weight"], p["time_mlp.0.bias"], tf32=t32)),
+                    p["time_mlp.2.weight"], p["time_mlp.2.bias"], tf32=t32)
 
     def run_layer(x, kind, i, depth, heads, res):
         for j in range(depth):
@@ -199,14 +241,14 @@ def backbone_forward(x, lead_time: timedelta, patch_res, p, *, embed_dim, encode
         x = run_layer(x, "encoder", i, encoder_depths[i], encoder_num_heads[i], all_res[i])
         skips.append(x)
         if i < n_enc - 1:
-            x = patch_merge(x, all_res[i], p, f"encoder_layers.{i}.downsample.")
+            x = patch_merge(x, all_res[i], p, f"encoder_layers.{i}.downsample.", tf32=bf16_mixed)
         if trace is not None:
             trace[f"enc{i}_out"] = x
     for i in range(n_dec):
         index = n_dec - i - 1
         x = run_layer(x, "decoder", i, decoder_depths[i], decoder_num_heads[i], all_res[index])
         if i < n_dec - 1:
-            x = patch_split(x, all_res[index], padded[index - 1], p, f"decoder_layers.{i}.upsample.")
+            x = patch_split(x, all_res[index], padded[index - 1], p, f"decoder_layers.{i}.upsample.", tf32=bf16_mixed)
         if 0 < i < n_dec - 1:
             x = x + skips[index - 1]
             tag = f"dec{i}_skip_add"

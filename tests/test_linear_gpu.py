@@ -7,6 +7,7 @@ largest output plus the fp32 accumulation error."""
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import pytest
@@ -27,9 +28,13 @@ def _ref(x, w, b, act):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1000, 512, 512), (4099, 2048, 512), (259, 1536, 1024),
-                                   (16200, 768, 128)])
+                                   (16200, 768, 128), (300, 256, 2048), (64, 512, 1024)])
 @pytest.mark.parametrize("act", ["gelu", "none"])
-def test_linear_bias_act_matches_float64(M, N, K, act):
+@pytest.mark.parametrize("kernel", ["single", "pair"])
+def test_linear_bias_act_matches_float64(M, N, K, act, kernel, monkeypatch):
+    """Both kernels (single CTA, 128 x 256 tiles; CTA pair, 256 x 256 tiles), including M tails
+    that leave the odd CTA of the last pair without a single row."""
+    monkeypatch.setenv("FA_GEMM_KERNEL", kernel)
     g = torch.Generator().manual_seed(M + N + K)
     x = torch.randn(M, K, generator=g).bfloat16().cuda()
     w = (torch.randn(N, K, generator=g) * 0.05).bfloat16().cuda()
@@ -46,6 +51,25 @@ def test_linear_bias_act_matches_float64(M, N, K, act):
     rel = (err.norm() / ref.norm()).item()
     rel_unfused = ((unfused - ref).norm() / ref.norm()).item()
     assert rel <= max(rel_unfused * 1.05, 2e-3)
+    st = ctypes.c_int(-1)
+    _lib.check(_lib.load().fa_gemm_status(ctypes.byref(st)), "status")
+    assert st.value == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(259200, 2048, 512), (64800, 4096, 1024), (16200, 8192, 2048)])
+def test_pair_and_single_kernels_agree_at_config4_shapes(M, N, K, monkeypatch):
+    """At the config-4 fc1 shapes the two kernels accumulate the same products in the same K
+    order (16-wide UMMA steps), so their outputs are identical."""
+    g = torch.Generator(device="cuda").manual_seed(K)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).bfloat16()
+    b = (torch.randn(N, device="cuda", generator=g) * 0.02).bfloat16()
+    outs = []
+    for kernel in ("single", "pair"):
+        monkeypatch.setenv("FA_GEMM_KERNEL", kernel)
+        outs.append(linear_bias_act(x, w, b, act="gelu"))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
 
 
 def test_linear_bias_act_batched_input_and_strided_rows():
