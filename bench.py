@@ -240,6 +240,8 @@ OPERATORS = {
     "fc2_gemm": ("tensor", "cuBLAS bf16 GEMM"),
     "adaln2_partition": ("hbm", "this library: adaln_kernel (next-partition fused)"),
     "adaln2": ("hbm", "this library: adaln_kernel"),
+    "proj_adaln1": ("tensor+hbm", "this library: proj GEMM + unmerge + AdaLN1 + residual in one kernel (CTA pair)"),
+    "fc2_adaln2": ("tensor+hbm", "this library: fc2 GEMM + AdaLN2 + residual (+ next partition) in one kernel (CTA pair)"),
 }
 # DRAM bytes / algorithmic bytes from ncu captures of the kernel (profiles/): the attention at
 # config 2 and the fused fc1 + GELU at the config-4 stage-1 shape.
@@ -263,6 +265,13 @@ def step_breakdown(summary: dict, step_ms: float, hbm: float, tf_sus: float, tf_
             tf = v["flops_per_step"] / (ms * 1e-3) / 1e12 if ms > 0 else 0.0
             row.update({"achieved": round(tf, 1), "unit": "TFLOP/s", "peak": tf_sus, "peak_kind": tf_kind,
                         "frac": round(tf / tf_sus, 3)})
+        elif bound == "tensor+hbm":
+            # A GEMM whose epilogue carries a memory-bound op: both roofs, the higher fraction binds.
+            tf = v["flops_per_step"] / (ms * 1e-3) / 1e12 if ms > 0 else 0.0
+            gbs = v["bytes_per_step"] / (ms * 1e-3) / 1e9 if ms > 0 else 0.0
+            row.update({"achieved": round(tf, 1), "unit": "TFLOP/s", "peak": tf_sus, "peak_kind": tf_kind,
+                        "frac_tensor": round(tf / tf_sus, 3), "achieved_gbs": round(gbs, 1), "hbm_peak": hbm,
+                        "frac_hbm": round(gbs / hbm, 3), "frac": round(max(tf / tf_sus, gbs / hbm), 3)})
         else:
             gbs = v["bytes_per_step"] / (ms * 1e-3) / 1e9 if ms > 0 else 0.0
             row.update({"achieved": round(gbs, 1), "unit": "GB/s", "peak": hbm, "peak_kind": peak_kind,

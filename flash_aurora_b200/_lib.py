@@ -24,6 +24,7 @@ FA_GELU_ERFF, FA_GELU_POLY = 0, 1
 FA_ATTN_FLAG_REGIONS_FIT = 1
 FA_ACT_NONE, FA_ACT_GELU = 0, 1
 FA_STATUS_REGIONS_BROKEN, FA_STATUS_WATCHDOG_SELFTEST = 28, 90
+FA_ROWS_TOKENS, FA_ROWS_WINDOWS = 0, 1
 
 _i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p
 _u32 = ctypes.c_uint
@@ -67,6 +68,8 @@ SIGNATURES = {
     "fa_attention_status": (_i32, [ctypes.POINTER(ctypes.c_int)]),
     "fa_attention_status_reset": (_i32, [_vp]),
     "fa_watchdog_selftest": (_i32, [_i64, _vp]),
+    "fa_linear_adaln_film": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _f32, _f32, _vp, _vp, _vp, _vp,
+                                    _i64, _i64, _i64, _i64, _i32p, _i32p, _i32p, _vp]),
 }
 
 _lib = None

@@ -46,7 +46,7 @@ from .adaln import (
 from . import _lib
 from . import recorder as _rec
 from .activation import gelu_erf
-from .linear import linear_bias_act
+from .linear import linear_adaln_film_add_residual, linear_bias_act
 from .sharding import BandContext
 from .swin3d_layout import band_halo_extract, roll_pad_partition_windows, roll_pad_partition_windows_band
 from .util import maybe_adjust_windows, window_geometry
@@ -68,6 +68,9 @@ __all__ = [
 ]
 
 PRECISIONS = ("bf16_mixed", "tf32", "fp32")
+# In bf16_mixed at D = 512 the proj -> norm1 and fc2 -> norm2 pairs run as one kernel each
+# (fa_linear_adaln_film); the split path computes the same values bit for bit (tests compare them).
+FUSE_LINEAR_ADALN = True
 
 
 def _check_precision(p: str) -> str:
@@ -266,12 +269,24 @@ class Swin3DTransformerBlock(nn.Module):
             Nw = xw.shape[1]
             _rec.end("attention", ev, 4 * T * D * e, 4 * xw.shape[0] * heads * Nw * Nw * (D // heads))
             wp, bp = self._w(self.attn.proj, bf16)
-            ev = _rec.begin()
-            a = self._linear(a, wp, bp, bf16)
-            _rec.end("proj_gemm", ev, (2 * T * D + D * D) * e, 2 * T * D * D)
             x1_bf16 = torch.empty(B, L, D, device=x.device, dtype=torch.bfloat16) if bf16 else None
+            fuse = FUSE_LINEAR_ADALN and bf16 and band is None and D == 512 and bp is not None
+            if fuse:
+                # proj + crop/un-roll/merge + norm1 + residual in one kernel (the proj output stays
+                # on chip); also writes the bf16 copy of x1 for fc1.
+                ev = _rec.begin()
+                x1 = linear_adaln_film_add_residual(
+                    a, wp, bp, x, sc1, sh1, res, self.window_size, self.shift_size, rows="windows",
+                    scale_bias=float(self.norm1.scale_bias), eps=eps, out_bf16=x1_bf16)
+                _rec.end("proj_adaln1", ev, (T * D + D * D) * e + B * L * D * (4 + 4 + 2), 2 * T * D * D)
+            else:
+                ev = _rec.begin()
+                a = self._linear(a, wp, bp, bf16)
+                _rec.end("proj_gemm", ev, (2 * T * D + D * D) * e, 2 * T * D * D)
             ev = _rec.begin()
-            if band is None:
+            if fuse:
+                pass
+            elif band is None:
                 x1 = unmerge_adaptive_layernorm_film_add_residual(
                     a, x, sc1, sh1, res, self.window_size, self.shift_size, float(self.norm1.scale_bias), eps,
                     out_bf16=x1_bf16)
@@ -284,8 +299,9 @@ class Swin3DTransformerBlock(nn.Module):
                 x1 = unmerge_adaptive_layernorm_film_add_residual_band(
                     a, halo_in, x, sc1, sh1, res, field_res, self.window_size, self.shift_size,
                     float(self.norm1.scale_bias), eps, out_bf16=x1_bf16)
-            # windows (non-pad tokens) + fp32 residual read, fp32 output (+ bf16 copy) written
-            _rec.end("adaln1_unmerge", ev, B * L * D * (e + 4 + 4 + (2 if bf16 else 0)))
+            if not fuse:
+                # windows (non-pad tokens) + fp32 residual read, fp32 output (+ bf16 copy) written
+                _rec.end("adaln1_unmerge", ev, B * L * D * (e + 4 + 4 + (2 if bf16 else 0)))
             w1, b1 = self._w(self.mlp.fc1, bf16)
             hid = w1.shape[0]
             ev = _rec.begin()
@@ -297,6 +313,18 @@ class Swin3DTransformerBlock(nn.Module):
                 h = gelu_erf(h, inplace=True)
             _rec.end("fc1_gelu_gemm", ev, (B * L * D + hid * D + B * L * hid) * e, 2 * B * L * D * hid)
             w2, b2 = self._w(self.mlp.fc2, bf16)
+            if fuse:
+                # fc2 + norm2 + residual (+ the next block's partition) in one kernel.
+                ev = _rec.begin()
+                nxt = None
+                if next_windows is not None:
+                    nxt = next_windows
+                y = linear_adaln_film_add_residual(
+                    h, w2, b2, x1, sc2, sh2, res, self.window_size, self.shift_size, rows="tokens",
+                    scale_bias=float(self.norm2.scale_bias), eps=eps, next_windows=nxt)
+                _rec.end("fc2_adaln2", ev, (B * L * hid + hid * D) * e + B * L * D * (4 + 4 + (2 if nxt else 0)),
+                         2 * B * L * D * hid)
+                return y
             ev = _rec.begin()
             h = F.linear(h, w2, b2)
             _rec.end("fc2_gemm", ev, (B * L * hid + hid * D + B * L * D) * e, 2 * B * L * D * hid)

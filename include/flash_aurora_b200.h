@@ -282,6 +282,34 @@ int fa_layernorm_affine(const void* x, int x_dtype, const void* residual, const 
 int fa_attention_status(int* status_out);
 int fa_attention_status_reset(void* stream);
 
+/* Row kinds of fa_linear_adaln_film. */
+enum { FA_ROWS_TOKENS = 0, FA_ROWS_WINDOWS = 1 };
+
+/*
+ * A bf16 linear with D = 512 output features whose rows are layer-normalised, FiLM-modulated and
+ * added to the fp32 residual stream in the same kernel (the output h of the linear never reaches
+ * HBM):
+ *   h[m]    = bf16(a[m] . w^T + bias)           a (M, K) bf16 (row stride lda), w (512, K), bias (512) bf16
+ *   out[t]  = residual[t] + LN(h[m]) * (scale_bias + scale[b]) + shift[b]     (fp32, eps as given)
+ * scale / shift are fp32 (B, 512); residual / out fp32 (B * C*H*W, 512) token rows (out must not
+ * alias residual). Replaces the linear + AdaLN pairs of the Swin3D block (swin3d.py:706-815,
+ * film.py:101-139 / ops/triton_adaln.py:83-145 after ops/triton_swin3d_layout.py:124-189):
+ *   FA_ROWS_WINDOWS  rows m are the window slots of this block's geometry (window_size, shift_size),
+ *                    M = B * nW * N; token t = the slot's source token (pad slots write nothing):
+ *                    attention proj fused with crop/un-roll/unmerge + norm1. out_bf16 (nullable,
+ *                    (B * C*H*W, 512) bf16) receives a bf16 copy of out.
+ *   FA_ROWS_TOKENS   rows m are tokens, M = B * C*H*W: MLP fc2 + norm2. win_out (nullable, bf16)
+ *                    receives out in the window layout of a next block with next_shift_size (same
+ *                    window size); its pad slots are left untouched.
+ * K must be a multiple of 32; every pointer 16-byte aligned. Equals fa_linear_bias_act followed by
+ * fa_unmerge_adaln_film / fa_adaln_film(_partition) bit for bit.
+ */
+int fa_linear_adaln_film(const void* a, const void* w, const void* bias, int64_t M, int64_t K, int64_t lda,
+                         int rows_kind, const float* scale, const float* shift, float scale_bias, float eps,
+                         const float* residual, float* out, void* out_bf16, void* win_out, int64_t B,
+                         int64_t C, int64_t H, int64_t W, const int32_t window_size[3],
+                         const int32_t shift_size[3], const int32_t next_shift_size[3], void* stream);
+
 /* Device status codes with a fixed meaning (the other non-zero codes name the bounded wait of a
  * kernel that gave up). */
 enum {

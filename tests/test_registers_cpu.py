@@ -71,7 +71,15 @@ def test_adaln_vector_kernels_do_not_spill(tmp_path):
 
 def test_fused_gemm_does_not_spill(tmp_path):
     report = _ptxas_report("gemm.cu", tmp_path)
-    kernels = {k: v for k, v in report.items() if "gemm_bias_act_kernel" in k}
+    kernels = {k: v for k, v in report.items() if "gemm_bias_act_kernel" in k or "gemm_pair_bias_act_kernel" in k}
+    assert len(kernels) == 4, sorted(kernels)
+    spilled = {k: v for k, v in kernels.items() if v[1] > 0}
+    assert not spilled, spilled
+
+
+def test_gemm_adaln_does_not_spill(tmp_path):
+    report = _ptxas_report("gemm_adaln.cu", tmp_path)
+    kernels = {k: v for k, v in report.items() if "gemm_adaln_pair_kernel" in k}
     assert len(kernels) == 2, sorted(kernels)
     spilled = {k: v for k, v in kernels.items() if v[1] > 0}
     assert not spilled, spilled
