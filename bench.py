@@ -785,6 +785,51 @@ def run_gemm(args) -> None:
                           **{f"{k}_tflops": round(flops / (v * 1e-3) / 1e12, 1) for k, v in res.items()},
                           "peak": tf_peak, "peak_kind": kind}), flush=True)
         del a, w, b
+    run_fused_s1(args, flush, g)
+
+
+def run_fused_s1(args, flush=None, g=None) -> None:
+    """Stage 1 (D = 512): the fused linear + AdaLN kernel against the same linear on this library's
+    GEMM followed by the stand-alone AdaLN kernel (unmerge-fused for proj, next-partition-fused for
+    fc2), and against cuBLAS + AdaLN for fc2. A few GB on the device: small enough for an ncu
+    capture of one launch."""
+    import flash_aurora_b200 as fa
+    from flash_aurora_b200.adaln import adaptive_layernorm_film_add_residual_partition
+    from flash_aurora_b200.linear import linear_adaln_film_add_residual
+    dev = torch.device("cuda", 0)
+    flush = flush or L2Flush(dev)
+    g = g or torch.Generator(device=dev).manual_seed(0)
+    res, ws, ss = (4, 180, 360), (2, 6, 12), (1, 3, 6)
+    L, D = 4 * 180 * 360, 512
+    x = torch.randn(1, L, D, device=dev, generator=g)
+    sc = torch.randn(1, 1, D, device=dev, generator=g) * 0.1
+    sh = torch.randn(1, 1, D, device=dev, generator=g) * 0.1
+    wins = torch.randn(1800, 144, D, device=dev, generator=g).bfloat16()
+    wp = (torch.randn(D, D, device=dev, generator=g) * 0.02).bfloat16()
+    bp = (torch.randn(D, device=dev, generator=g) * 0.02).bfloat16()
+    xb = torch.empty(1, L, D, device=dev, dtype=torch.bfloat16)
+    fused = _time_launches(lambda: linear_adaln_film_add_residual(wins, wp, bp, x, sc, sh, res, ws, ss, rows="windows",
+                                                                  out_bf16=xb), args.steps, flush=flush)
+    split = _time_launches(lambda: fa.unmerge_adaptive_layernorm_film_add_residual(
+        fa.linear_bias_act(wins, wp, bp, act="none"), x, sc, sh, res, ws, ss, 0.0, 1e-5, out_bf16=xb),
+        args.steps, flush=flush)
+    print(json.dumps({"workload": "config4 S1 proj + unmerge + AdaLN1 + residual (+ bf16 copy)",
+                      "fused_ms": round(fused, 4), "split_ms": round(split, 4)}), flush=True)
+    del wins, wp, bp
+    hid = torch.randn(1, L, 4 * D, device=dev, generator=g).bfloat16()
+    w2 = (torch.randn(D, 4 * D, device=dev, generator=g) * 0.02).bfloat16()
+    b2 = (torch.randn(D, device=dev, generator=g) * 0.02).bfloat16()
+    nxt = torch.zeros(1800, 144, D, device=dev, dtype=torch.bfloat16)
+    fused = _time_launches(lambda: linear_adaln_film_add_residual(hid, w2, b2, x, sc, sh, res, ws, (0, 0, 0),
+                                                                  rows="tokens", next_windows=(ss, nxt)),
+                           args.steps, flush=flush)
+    split = _time_launches(lambda: adaptive_layernorm_film_add_residual_partition(
+        x, fa.linear_bias_act(hid, w2, b2, act="none"), sc, sh, res, ws, ss, nxt), args.steps, flush=flush)
+    cub = _time_launches(lambda: adaptive_layernorm_film_add_residual_partition(
+        x, torch.nn.functional.linear(hid, w2, b2), sc, sh, res, ws, ss, nxt), args.steps, flush=flush)
+    print(json.dumps({"workload": "config4 S1 fc2 + AdaLN2 + residual + next partition",
+                      "fused_ms": round(fused, 4), "split_ms": round(split, 4), "split_cublas_ms": round(cub, 4)}),
+          flush=True)
     from flash_aurora_b200.status import check_device_status
     check_device_status(dev)
 
@@ -798,7 +843,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sharded", action="store_true", help="skip the config-5 sharded-stage object")
     ap.add_argument("--no-bars", action="store_true", help="skip the same-box stock PyTorch comparison")
-    ap.add_argument("--workload", choices=["backbone", "attention", "layout_adaln", "adaln_stages", "sharded", "gemm"],
+    ap.add_argument("--workload", choices=["backbone", "attention", "layout_adaln", "adaln_stages", "sharded", "gemm",
+                                           "fused_s1"],
                     default="backbone")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -811,6 +857,8 @@ def main() -> None:
         return run_adaln_stages(args)
     if args.workload == "gemm":
         return run_gemm(args)
+    if args.workload == "fused_s1":
+        return run_fused_s1(args)
     if args.workload == "sharded" and args.impl != "reference":
         return run_sharded(args)
     if args.impl == "reference":

@@ -289,66 +289,102 @@ gemm_adaln_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_con
       }
       epi_bar();  // every row of the h tile is written
       prefetch_tile(j + 1);
-      // E2: AdaLN + residual, 16 rows per warp; lane l holds columns 8l..8l+7 and 256+8l..+7.
+      // E2: AdaLN + residual, 16 rows per warp in groups of 4; lane l holds columns 8l..8l+7 and
+      // 256+8l..+7 of a row. A group's residual loads are issued first and its four row reductions
+      // are interleaved, so one memory round trip and one reduction chain serve four rows; the
+      // arithmetic of each row is the stand-alone AdaLN kernel's, in the same order. The bf16 row
+      // values are re-read from the h tile for each pass (three 1 KB shared-memory reads per row)
+      // instead of being held for all four rows.
 #pragma unroll 1
-      for (int i = 0; i < 16; ++i) {
-        const int r = e * 16 + i;
-        const int64_t m = m0 + r;
-        const int64_t tok = token_of(m);
-        if (tok < 0) continue;
-        const int64_t b = kMode == kRowsTokens ? tok / p.L : m / p.slots;
-        float v[2][8];
+      for (int i0 = 0; i0 < 16; i0 += 4) {
+        int32_t tok[4], bb[4];  // token rows and batch indices fit 32 bits (M < 2^31 is checked)
+        float rr[4][16];
 #pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
-          uint32_t w0, w1, w2, w3;
-          ld_shared_v4(sh_tile + h_off(r, ch * 32 + lane), w0, w1, w2, w3);
-          const uint32_t ws[4] = {w0, w1, w2, w3};
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float2 f = unpack_bf16x2(ws[u]);
-            v[ch][2 * u] = f.x;
-            v[ch][2 * u + 1] = f.y;
+        for (int k = 0; k < 4; ++k) {
+          const int64_t m = m0 + e * 16 + i0 + k;
+          tok[k] = (int32_t)token_of(m);
+          bb[k] = tok[k] < 0 ? 0 : (int32_t)(kMode == kRowsTokens ? tok[k] / p.L : m / p.slots);
+          if (tok[k] >= 0) {
+            Vec8<float>::load_stream(p.residual + (int64_t)tok[k] * kD + lane * 8, rr[k]);
+            Vec8<float>::load_stream(p.residual + (int64_t)tok[k] * kD + 256 + lane * 8, rr[k] + 8);
           }
         }
-        float s = 0.f;
+        // Row values are re-read from the h tile for each pass instead of held for four rows.
+        auto load_row = [&](int r, float (&v)[16]) {
 #pragma unroll
-        for (int ch = 0; ch < 2; ++ch)
+          for (int ch = 0; ch < 2; ++ch) {
+            uint32_t w0, w1, w2, w3;
+            ld_shared_v4(sh_tile + h_off(r, ch * 32 + lane), w0, w1, w2, w3);
+            const uint32_t ws[4] = {w0, w1, w2, w3};
 #pragma unroll
-          for (int u = 0; u < 8; ++u) s += v[ch][u];
-        const float mean = warp_sum(s) * inv_d;
-        float qd = 0.f;
-#pragma unroll
-        for (int ch = 0; ch < 2; ++ch)
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float d = v[ch][u] - mean;
-            qd += d * d;
+            for (int u = 0; u < 4; ++u) {
+              const float2 f = unpack_bf16x2(ws[u]);
+              v[8 * ch + 2 * u] = f.x;
+              v[8 * ch + 2 * u + 1] = f.y;
+            }
           }
-        const float rstd = rsqrtf(warp_sum(qd) * inv_d + p.eps);
-        int64_t wrow = -1;
-        if constexpr (kMode == kRowsTokens) {
-          if (p.win_out) {
-            const int32_t t = (int32_t)(tok - b * p.L);
-            const int32_t w = t % p.wlp.W;
-            const int32_t hh = (t / p.wlp.W) % p.wlp.H;
-            const int32_t cc = t / (p.wlp.W * p.wlp.H);
-            wrow = b * (int64_t)p.wlp.nW * p.wlp.N + unmerge_slot(p.wlp, cc, hh, w);
+        };
+        float sm[4], mean[4], qd[4], rstd[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float v[16];
+          load_row(e * 16 + i0 + k, v);
+          sm[k] = 0.f;
+#pragma unroll
+          for (int u = 0; u < 16; ++u) sm[k] += v[u];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) sm[k] += __shfl_xor_sync(0xffffffffu, sm[k], o);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float v[16];
+          load_row(e * 16 + i0 + k, v);
+          mean[k] = sm[k] * inv_d;
+          qd[k] = 0.f;
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const float d = v[u] - mean[k];
+            qd[k] += d * d;
           }
         }
 #pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
-          const int col = (ch * 32 + lane) * 8;
-          float sc[8], sf[8], rr[8], y[8];
-          Vec8<float>::load(p.scale + b * kD + col, sc);
-          Vec8<float>::load(p.shift + b * kD + col, sf);
+        for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-          for (int u = 0; u < 8; ++u) y[u] = (v[ch][u] - mean) * rstd * (p.scale_bias + sc[u]) + sf[u];
-          Vec8<float>::load_stream(p.residual + tok * kD + col, rr);
+          for (int k = 0; k < 4; ++k) qd[k] += __shfl_xor_sync(0xffffffffu, qd[k], o);
 #pragma unroll
-          for (int u = 0; u < 8; ++u) y[u] += rr[u];
-          Vec8<float>::store(p.out + tok * kD + col, y);
-          if (p.out_bf16) Vec8<__nv_bfloat16>::store(p.out_bf16 + tok * kD + col, y);
-          if (wrow >= 0) Vec8<__nv_bfloat16>::store(p.win_out + wrow * kD + col, y);
+        for (int k = 0; k < 4; ++k) rstd[k] = rsqrtf(qd[k] * inv_d + p.eps);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (tok[k] < 0) continue;
+          float v[16];
+          load_row(e * 16 + i0 + k, v);
+          int64_t wrow = -1;
+          if constexpr (kMode == kRowsTokens) {
+            if (p.win_out) {
+              const int32_t t = (int32_t)(tok[k] - (int64_t)bb[k] * p.L);
+              const int32_t w = t % p.wlp.W;
+              const int32_t hh = (t / p.wlp.W) % p.wlp.H;
+              const int32_t cc = t / (p.wlp.W * p.wlp.H);
+              wrow = bb[k] * (int64_t)p.wlp.nW * p.wlp.N + unmerge_slot(p.wlp, cc, hh, w);
+            }
+          }
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch) {
+            const int col = (ch * 32 + lane) * 8;
+            float sc[8], sf[8], y[8];
+            Vec8<float>::load(p.scale + (int64_t)bb[k] * kD + col, sc);
+            Vec8<float>::load(p.shift + (int64_t)bb[k] * kD + col, sf);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              y[u] = (v[8 * ch + u] - mean[k]) * rstd[k] * (p.scale_bias + sc[u]) + sf[u];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) y[u] += rr[k][8 * ch + u];
+            Vec8<float>::store(p.out + (int64_t)tok[k] * kD + col, y);
+            if (p.out_bf16) Vec8<__nv_bfloat16>::store(p.out_bf16 + (int64_t)tok[k] * kD + col, y);
+            if (wrow >= 0) Vec8<__nv_bfloat16>::store(p.win_out + wrow * kD + col, y);
+          }
         }
       }
       epi_bar();  // the h tile is free for the next E1
