@@ -1,6 +1,7 @@
 // Host-side helpers of the C ABI: error strings, window geometry, shifted-window region ids.
 #include <algorithm>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -20,6 +21,35 @@ int check_launch(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(FA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
   return FA_OK;
+}
+
+int max_resident_pairs(const void* kernel, int threads, int smem_bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return num_sms() / 2;
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(kernel, dev);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(num_sms() & ~1));
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = (size_t)smem_bytes;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters <= 0) {
+    cudaGetLastError();  // clear the error of the query; fall back to every SM pair
+    clusters = num_sms() / 2;
+  }
+  cache[key] = clusters;
+  return clusters;
 }
 
 int num_sms() {

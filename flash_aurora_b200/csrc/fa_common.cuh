@@ -243,5 +243,10 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int num_sms();  // SM count of the current device (cached per device)
+// CTA pairs (clusters of 2) of `kernel` that fit on the current device at once, for a persistent
+// grid of one pair per slot (cached per kernel and device; the GPC layout can leave an SM without a
+// partner, so this can be below num_sms() / 2). The kernel's dynamic shared memory attribute must
+// already be set.
+int max_resident_pairs(const void* kernel, int threads, int smem_bytes);
 
 }  // namespace fa

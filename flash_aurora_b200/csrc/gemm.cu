@@ -512,7 +512,7 @@ extern "C" int fa_linear_bias_act(const void* a, const void* w, const void* bias
   if (use_pair) {
     auto kern = act == FA_ACT_GELU ? gemm::gemm_pair_bias_act_kernel<true> : gemm::gemm_pair_bias_act_kernel<false>;
     FA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::kPairSmem));
-    const int pairs_max = num_sms() / 2;
+    const int pairs_max = max_resident_pairs((const void*)kern, gemm::kThreads, gemm::kPairSmem);
     const int pairs = p.num_tiles < pairs_max ? p.num_tiles : pairs_max;
     kern<<<2 * pairs, gemm::kThreads, gemm::kPairSmem, (cudaStream_t)stream>>>(ma, mw, mo, p);
     return check_launch("gemm_pair_bias_act_kernel");

@@ -26,11 +26,14 @@
 //                   plain linear rounds its output, written to a 128 x 512 bf16 tile in shared
 //                   memory (16-byte chunks XOR-swizzled by row); then the TMEM is released, so
 //                   the next tile's UMMAs run during E2.
-//               E2  warp = row: the AdaLN + residual of 16 rows per warp with the arithmetic of
-//                   the stand-alone AdaLN kernel for D = 512 (same element-to-lane assignment,
-//                   same two-pass fp32 reductions), so the result equals the unfused pair bit
-//                   for bit; coalesced 16-byte row I/O; the next tile's residual rows are
-//                   prefetched into L2.
+//                   Each thread also sums its half row.
+//               E1b thread = row (four warps): mean from the half-row sums, then the sum of squared
+//                   deviations over the bf16 row in shared memory (two-pass variance, fp32).
+//               E2  warp = row: y = residual + (h - mean) * rstd * (scale_bias + scale) + shift,
+//                   coalesced 16-byte row I/O, four rows' residual loads in flight per warp; the
+//                   next tile's residual rows are prefetched into L2.
+// The row statistics are summed in another order than the stand-alone AdaLN kernel's warp
+// reduction, so results agree with the unfused pair to fp32 rounding, not bit for bit.
 // Every mbarrier wait is bounded (status codes 18-23 in the GEMM status word).
 #include <cudaTypedefs.h>
 
@@ -60,7 +63,8 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr uint32_t kTmemCols = 512;
 constexpr int kNumBars = 2 * kStages + 3;
-constexpr int kSmem = kStages * kStageBytes + kHBytes + kNumBars * 8 + 16 + 1024;
+constexpr int kStatBytes = 3 * kRows * 4;  // per row: two half-row sums, then mean and rstd
+constexpr int kSmem = kStages * kStageBytes + kHBytes + kStatBytes + kNumBars * 8 + 16 + 1024;
 static_assert(kSmem <= 227 * 1024, "shared memory budget");
 constexpr uint32_t kIdesc = make_idesc(1, 256, 256, false, false);
 constexpr uint64_t kTimeoutNs = 2000000000ull;
@@ -129,7 +133,8 @@ gemm_adaln_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_con
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t sh_tile = sbase + kStages * kStageBytes;  // h tile (1024-aligned)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kHBytes);
+  float* stat = reinterpret_cast<float*>(smem + kStages * kStageBytes + kHBytes);  // [3][kRows]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kHBytes + kStatBytes);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
   const uint32_t bar0 = smem_u32(bars);
   auto BAR = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
@@ -254,7 +259,8 @@ gemm_adaln_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_con
       const bool ready = mbar_wait(BAR(kAccFull), (uint32_t)(j & 1), abort, p.status, 23, kTimeoutNs);
       if (!epi_all(ready)) break;
       tc_fence_after();
-      // E1: accumulators + bias -> bf16 row tile.
+      // E1: accumulators + bias -> bf16 row tile, and this thread's half-row sum of the bf16 values.
+      float acc4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
       for (int c = 0; c < 256; c += 64) {
         uint32_t v0[32], v1[32];
@@ -276,10 +282,13 @@ gemm_adaln_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_con
             const int si = idx & 31;
             const float2 bf = unpack_bf16x2(bb[u]);
             pk[u] = pack_bf16x2(__uint_as_float(src[si]) + bf.x, __uint_as_float(src[si + 1]) + bf.y);
+            const float2 hv = unpack_bf16x2(pk[u]);
+            acc4[u] += hv.x + hv.y;
           }
           st_shared_v4(sh_tile + h_off(r1, col / 8 + v), pk[0], pk[1], pk[2], pk[3]);
         }
       }
+      stat[half * kRows + r1] = (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
       // The accumulator is read: release it (the next tile's UMMAs start during E2).
       tc_fence_before();
       __syncwarp();
@@ -287,14 +296,33 @@ gemm_adaln_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_con
         if (rank == 0) mbar_arrive(BAR(kAccEmpty));
         else mbar_arrive_remote(map_shared_rank(BAR(kAccEmpty), 0));
       }
-      epi_bar();  // every row of the h tile is written
+      epi_bar();  // every row of the h tile and every half-row sum is written
       prefetch_tile(j + 1);
-      // E2: AdaLN + residual, 16 rows per warp in groups of 4; lane l holds columns 8l..8l+7 and
-      // 256+8l..+7 of a row. A group's residual loads are issued first and its four row reductions
-      // are interleaved, so one memory round trip and one reduction chain serve four rows; the
-      // arithmetic of each row is the stand-alone AdaLN kernel's, in the same order. The bf16 row
-      // values are re-read from the h tile for each pass (three 1 KB shared-memory reads per row)
-      // instead of being held for all four rows.
+      // E1b (thread = row, the four half-0 warps): mean from the two half-row sums, then the sum
+      // of squared deviations over the whole bf16 row from shared memory (two-pass variance).
+      if (half == 0) {
+        const float mean = (stat[r1] + stat[kRows + r1]) * inv_d;
+        float q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int jc = 0; jc < kD / 8; ++jc) {
+          uint32_t w0, w1, w2, w3;
+          ld_shared_v4(sh_tile + h_off(r1, jc), w0, w1, w2, w3);
+          const uint32_t ws[4] = {w0, w1, w2, w3};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float2 f = unpack_bf16x2(ws[u]);
+            const float d0 = f.x - mean, d1 = f.y - mean;
+            q4[u] = fmaf(d0, d0, q4[u]);
+            q4[u] = fmaf(d1, d1, q4[u]);
+          }
+        }
+        stat[2 * kRows + r1] = mean;
+        stat[r1] = rsqrtf(((q4[0] + q4[1]) + (q4[2] + q4[3])) * inv_d + p.eps);  // rstd
+      }
+      epi_bar();
+      // E2 (warp = row): y = residual + (h - mean) * rstd * (scale_bias + scale) + shift, 16 rows per
+      // warp in groups of 4 whose residual loads are issued together; lane l holds columns
+      // 8l..8l+7 and 256+8l..+7. Coalesced 16-byte row I/O, no reductions.
 #pragma unroll 1
       for (int i0 = 0; i0 < 16; i0 += 4) {
         int32_t tok[4], bb[4];  // token rows and batch indices fit 32 bits (M < 2^31 is checked)
@@ -309,57 +337,11 @@ gemm_adaln_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_con
             Vec8<float>::load_stream(p.residual + (int64_t)tok[k] * kD + 256 + lane * 8, rr[k] + 8);
           }
         }
-        // Row values are re-read from the h tile for each pass instead of held for four rows.
-        auto load_row = [&](int r, float (&v)[16]) {
-#pragma unroll
-          for (int ch = 0; ch < 2; ++ch) {
-            uint32_t w0, w1, w2, w3;
-            ld_shared_v4(sh_tile + h_off(r, ch * 32 + lane), w0, w1, w2, w3);
-            const uint32_t ws[4] = {w0, w1, w2, w3};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const float2 f = unpack_bf16x2(ws[u]);
-              v[8 * ch + 2 * u] = f.x;
-              v[8 * ch + 2 * u + 1] = f.y;
-            }
-          }
-        };
-        float sm[4], mean[4], qd[4], rstd[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          float v[16];
-          load_row(e * 16 + i0 + k, v);
-          sm[k] = 0.f;
-#pragma unroll
-          for (int u = 0; u < 16; ++u) sm[k] += v[u];
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-          for (int k = 0; k < 4; ++k) sm[k] += __shfl_xor_sync(0xffffffffu, sm[k], o);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          float v[16];
-          load_row(e * 16 + i0 + k, v);
-          mean[k] = sm[k] * inv_d;
-          qd[k] = 0.f;
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const float d = v[u] - mean[k];
-            qd[k] += d * d;
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-          for (int k = 0; k < 4; ++k) qd[k] += __shfl_xor_sync(0xffffffffu, qd[k], o);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) rstd[k] = rsqrtf(qd[k] * inv_d + p.eps);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           if (tok[k] < 0) continue;
-          float v[16];
-          load_row(e * 16 + i0 + k, v);
+          const int r = e * 16 + i0 + k;
+          const float mean = stat[2 * kRows + r], rstd = stat[r];
           int64_t wrow = -1;
           if constexpr (kMode == kRowsTokens) {
             if (p.win_out) {
@@ -373,12 +355,18 @@ gemm_adaln_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_con
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) {
             const int col = (ch * 32 + lane) * 8;
+            uint32_t w0, w1, w2, w3;
+            ld_shared_v4(sh_tile + h_off(r, ch * 32 + lane), w0, w1, w2, w3);
+            const uint32_t ws[4] = {w0, w1, w2, w3};
             float sc[8], sf[8], y[8];
             Vec8<float>::load(p.scale + (int64_t)bb[k] * kD + col, sc);
             Vec8<float>::load(p.shift + (int64_t)bb[k] * kD + col, sf);
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-              y[u] = (v[8 * ch + u] - mean[k]) * rstd[k] * (p.scale_bias + sc[u]) + sf[u];
+            for (int u = 0; u < 4; ++u) {
+              const float2 f = unpack_bf16x2(ws[u]);
+              y[2 * u] = (f.x - mean) * rstd * (p.scale_bias + sc[2 * u]) + sf[2 * u];
+              y[2 * u + 1] = (f.y - mean) * rstd * (p.scale_bias + sc[2 * u + 1]) + sf[2 * u + 1];
+            }
 #pragma unroll
             for (int u = 0; u < 8; ++u) y[u] += rr[k][8 * ch + u];
             Vec8<float>::store(p.out + (int64_t)tok[k] * kD + col, y);
@@ -492,7 +480,7 @@ extern "C" int fa_linear_adaln_film(const void* a, const void* w, const void* bi
   auto kern = rows_kind == FA_ROWS_TOKENS ? G::gemm_adaln_pair_kernel<G::kRowsTokens>
                                           : G::gemm_adaln_pair_kernel<G::kRowsWindows>;
   FA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem));
-  const int pairs_max = num_sms() / 2;
+  const int pairs_max = max_resident_pairs((const void*)kern, G::kThreads, G::kSmem);
   const int pairs = p.num_tiles < pairs_max ? p.num_tiles : pairs_max;
   kern<<<2 * pairs, G::kThreads, G::kSmem, (cudaStream_t)stream>>>(ma, mw, p);
   return check_launch("gemm_adaln_pair_kernel");

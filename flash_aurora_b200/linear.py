@@ -81,7 +81,7 @@ def linear_adaln_film_add_residual(
     (next_shift, buffer)`` also writes the result in bf16 into the window layout of a following
     block. ``residual`` is ``(B, L, 512)`` fp32, ``scale``/``shift`` ``(B, 1, 512)`` fp32.
     Returns the fp32 ``(B, L, 512)`` result. Equals ``linear_bias_act`` followed by the matching
-    AdaLN op bit for bit.
+    AdaLN op up to the summation order of the fp32 row statistics.
     """
     if rows not in _ROWS:
         raise ValueError(f"rows must be one of {tuple(_ROWS)}")

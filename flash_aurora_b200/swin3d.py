@@ -8,16 +8,18 @@ path (the upstream pure-PyTorch path is the test oracle, not part of this packag
 
 Per block (upstream swin3d.py:706-815, post-norm), precision ``"bf16_mixed"``:
 
-1. ``fa_roll_pad_partition``: fp32 residual -> bf16 windows (shift + pad + partition + cast).
-2. QKV linear, bf16 in/out (``fa_linear_bias_act``: tcgen05 GEMM, bias epilogue).
+1. ``fa_roll_pad_partition``: fp32 residual -> bf16 windows (shift + pad + partition + cast); inside a
+   stage the previous block's norm2 already wrote them (``fa_adaln_film_partition``).
+2. QKV linear, bf16 in/out (``fa_linear_bias_act``: tcgen05 GEMM, CTA pair, bias epilogue).
 3. ``fa_window_attention_qkvpacked``: bf16 window attention reading the packed QKV, shifted
    blocks masked by region ids, output in the (window, token, channel) layout.
 4. proj linear, bf16 (``fa_linear_bias_act``).
 5. ``fa_unmerge_adaln_film``: crop/un-roll/merge of the proj output fused into
    ``x1 = x + AdaLN1(.)`` (fp32), plus a bf16 copy of ``x1`` for fc1.
-6. ``fa_linear_bias_act``: fc1 + bias + exact GELU in one tcgen05 kernel (bf16 out) -> fc2 (bf16,
-   cuBLAS).
-7. ``fa_adaln_film``: ``x2 = x1 + AdaLN2(h)`` (bf16 input, fp32 residual and output).
+6. ``fa_linear_bias_act``: fc1 + bias + exact GELU in one tcgen05 kernel (bf16 out).
+7. fc2 + ``x2 = x1 + AdaLN2(h)`` (+ the next block's partition): at D = 512 one kernel
+   (``fa_linear_adaln_film``, the fc2 output never reaches HBM); elsewhere cuBLAS fc2 (faster than
+   the library GEMM at those shapes) then ``fa_adaln_film(_partition)``.
 
 Every rounding point equals the upstream ``bf16_mixed`` tier (custom_op_paths.py:188-263): the
 windows and ``x1`` are rounded to bf16 exactly where upstream autocast casts them, and the
@@ -68,9 +70,14 @@ __all__ = [
 ]
 
 PRECISIONS = ("bf16_mixed", "tf32", "fp32")
-# In bf16_mixed at D = 512 the proj -> norm1 and fc2 -> norm2 pairs run as one kernel each
-# (fa_linear_adaln_film); the split path computes the same values bit for bit (tests compare them).
-FUSE_LINEAR_ADALN = True
+# In bf16_mixed at D = 512 the fc2 -> norm2 (-> next partition) pair runs as one kernel
+# (fa_linear_adaln_film, token rows): measured 3-4 % faster than the pair at config-4 stage 1. The
+# same kernel also fuses proj -> unmerge -> norm1 (window rows), but that form measured slower than
+# the split pair (0.55-0.62 against 0.38-0.46 ms: its AdaLN phase, 8 warps per SM, is latency-bound
+# while a K = 512 GEMM has little tensor work to hide it under), so the block keeps the split pair
+# there. Both forms equal the split path up to the summation order of the fp32 row statistics.
+FUSE_FC2_ADALN = True
+FUSE_PROJ_ADALN = False
 
 
 def _check_precision(p: str) -> str:
@@ -270,7 +277,8 @@ class Swin3DTransformerBlock(nn.Module):
             _rec.end("attention", ev, 4 * T * D * e, 4 * xw.shape[0] * heads * Nw * Nw * (D // heads))
             wp, bp = self._w(self.attn.proj, bf16)
             x1_bf16 = torch.empty(B, L, D, device=x.device, dtype=torch.bfloat16) if bf16 else None
-            fuse = FUSE_LINEAR_ADALN and bf16 and band is None and D == 512 and bp is not None
+            fusable = bf16 and band is None and D == 512
+            fuse = FUSE_PROJ_ADALN and fusable and bp is not None
             if fuse:
                 # proj + crop/un-roll/merge + norm1 + residual in one kernel (the proj output stays
                 # on chip); also writes the bf16 copy of x1 for fc1.
@@ -313,7 +321,7 @@ class Swin3DTransformerBlock(nn.Module):
                 h = gelu_erf(h, inplace=True)
             _rec.end("fc1_gelu_gemm", ev, (B * L * D + hid * D + B * L * hid) * e, 2 * B * L * D * hid)
             w2, b2 = self._w(self.mlp.fc2, bf16)
-            if fuse:
+            if FUSE_FC2_ADALN and fusable and b2 is not None and w2.shape[1] % 32 == 0:
                 # fc2 + norm2 + residual (+ the next block's partition) in one kernel.
                 ev = _rec.begin()
                 nxt = None

@@ -302,7 +302,8 @@ enum { FA_ROWS_TOKENS = 0, FA_ROWS_WINDOWS = 1 };
  *                    receives out in the window layout of a next block with next_shift_size (same
  *                    window size); its pad slots are left untouched.
  * K must be a multiple of 32; every pointer 16-byte aligned. Equals fa_linear_bias_act followed by
- * fa_unmerge_adaln_film / fa_adaln_film(_partition) bit for bit.
+ * fa_unmerge_adaln_film / fa_adaln_film(_partition) up to the summation order of the fp32 row
+ * statistics (the linear's bf16 rounding is the same).
  */
 int fa_linear_adaln_film(const void* a, const void* w, const void* bias, int64_t M, int64_t K, int64_t lda,
                          int rows_kind, const float* scale, const float* shift, float scale_bias, float eps,

@@ -1,8 +1,9 @@
-"""The fused linear + AdaLN + residual kernel (``fa_linear_adaln_film``) equals the unfused pair
-(``linear_bias_act`` then the matching AdaLN op) bit for bit: same bf16 rounding of the linear's
-output, same fp32 two-pass row statistics. Both row kinds, padded and unpadded window grids, batch
-2, and M tails where the odd CTA of the last pair has no rows; plus the block with the fusion on
-and off."""
+"""The fused linear + AdaLN + residual kernel (``fa_linear_adaln_film``) against the unfused pair
+(``linear_bias_act`` then the matching AdaLN op). The linear's output is rounded to bf16 exactly as
+in the pair; the row statistics are fp32 two-pass in another summation order, so fp32 outputs agree
+to 2e-6 (relative and absolute) and bf16 outputs to one bf16 ulp on at most 0.1 % of the elements.
+Both row kinds, padded and unpadded window grids, batch 2, and M tails where the odd CTA of the
+last pair has no rows; plus the block with the fusion on and off."""
 
 from __future__ import annotations
 
@@ -16,6 +17,20 @@ from flash_aurora_b200.linear import linear_adaln_film_add_residual, linear_bias
 
 pytestmark = pytest.mark.gpu
 WS = (2, 6, 12)
+
+
+def _close_f32(got, want):
+    torch.testing.assert_close(got, want, rtol=2e-6, atol=2e-6)
+
+
+def _close_bf16(got, want):
+    """bf16 copies of fp32 values that agree to 2e-6: a rounding boundary between the two values
+    moves the result by one bf16 ulp (at most 2^-7 of the value), plus the fp32 difference."""
+    g, w = got.float(), want.float()
+    diff = (g - w).abs()
+    bound = w.abs() * 2 ** -7 + 4e-6
+    assert bool((diff <= bound).all()), float((diff / bound).max())
+    assert (diff > 0).float().mean().item() <= 1e-3
 
 
 def _mod(B, D, g):
@@ -41,8 +56,8 @@ def test_windows_rows_equal_proj_then_unmerge_adaln(res, shift, B):
     got_bf = torch.empty_like(want_bf)
     got = linear_adaln_film_add_residual(a, w, b, x, sc, sh, res, WS, shift, rows="windows", out_bf16=got_bf)
     fa.check_device_status()
-    assert torch.equal(got, want)
-    assert torch.equal(got_bf, want_bf)
+    _close_f32(got, want)
+    _close_bf16(got_bf, want_bf)
 
 
 @pytest.mark.parametrize("res,next_shift,K", [((4, 36, 72), (1, 3, 6), 2048), ((4, 45, 90), (0, 0, 0), 2048),
@@ -67,13 +82,16 @@ def test_token_rows_equal_fc2_then_adaln(res, next_shift, K):
         want = adaptive_layernorm_film_add_residual_partition(x1, y, sc, sh, res, WS, next_shift, wb_want)
         got = linear_adaln_film_add_residual(h, w, b, x1, sc, sh, res, WS, (0, 0, 0), rows="tokens",
                                              next_windows=(next_shift, wb_got))
-        assert torch.equal(wb_got, wb_want)
+        _close_bf16(wb_got, wb_want)
     fa.check_device_status()
-    assert torch.equal(got, want)
+    _close_f32(got, want)
 
 
+@pytest.mark.parametrize("flag", ["FUSE_FC2_ADALN", "FUSE_PROJ_ADALN"])
 @pytest.mark.parametrize("shift", [(0, 0, 0), (1, 3, 6)])
-def test_block_with_and_without_the_fusion(shift, monkeypatch):
+def test_block_with_and_without_the_fusion(shift, flag, monkeypatch):
+    """Each fused form of the block (fc2 -> norm2 is on by default, proj -> norm1 off) against the
+    split path."""
     torch.manual_seed(9)
     res = (4, 24, 48)
     blk = S.Swin3DTransformerBlock(dim=512, num_heads=8, time_dim=512, window_size=WS, shift_size=shift)
@@ -85,10 +103,15 @@ def test_block_with_and_without_the_fusion(shift, monkeypatch):
     x = torch.randn(1, 4 * 24 * 48, 512, generator=g).cuda()
     c = torch.randn(1, 512, generator=g).cuda()
     with torch.no_grad():
-        fused = blk(x, c, res)
-        monkeypatch.setattr(S, "FUSE_LINEAR_ADALN", False)
+        monkeypatch.setattr(S, "FUSE_FC2_ADALN", False)
+        monkeypatch.setattr(S, "FUSE_PROJ_ADALN", False)
         split = blk(x, c, res)
-    assert torch.equal(fused, split)
+        monkeypatch.setattr(S, flag, True)
+        fused = blk(x, c, res)
+    # norm1's output feeds fc1 through its bf16 copy, so a 1-ulp bf16 difference there reaches
+    # norm2: compare the block outputs in relative L2 (the bf16 tier's own drift is ~1e-3).
+    rel = ((fused - split).norm() / split.norm()).item()
+    assert rel <= 5e-5, rel
 
 
 def test_rejects_bad_arguments():
