@@ -18,8 +18,8 @@ Per block (upstream swin3d.py:706-815, post-norm), precision ``"bf16_mixed"``:
    ``x1 = x + AdaLN1(.)`` (fp32), plus a bf16 copy of ``x1`` for fc1.
 6. ``fa_linear_bias_act``: fc1 + bias + exact GELU in one tcgen05 kernel (bf16 out).
 7. fc2 + ``x2 = x1 + AdaLN2(h)`` (+ the next block's partition): at D = 512 one kernel
-   (``fa_linear_adaln_film``, the fc2 output never reaches HBM); elsewhere cuBLAS fc2 (faster than
-   the library GEMM at those shapes) then ``fa_adaln_film(_partition)``.
+   (``fa_linear_adaln_film``, the fc2 output never reaches HBM); elsewhere fc2 on the library GEMM
+   at K = 8192 and cuBLAS at K = 4096 (whichever measured faster), then ``fa_adaln_film(_partition)``.
 
 Every rounding point equals the upstream ``bf16_mixed`` tier (custom_op_paths.py:188-263): the
 windows and ``x1`` are rounded to bf16 exactly where upstream autocast casts them, and the
@@ -334,7 +334,11 @@ class Swin3DTransformerBlock(nn.Module):
                          2 * B * L * D * hid)
                 return y
             ev = _rec.begin()
-            h = F.linear(h, w2, b2)
+            if bf16 and b2 is not None and w2.shape[0] % 256 == 0 and w2.shape[1] >= 8192:
+                # Measured per stage: the library GEMM wins at K = 8192 (stage 3), cuBLAS at K = 4096.
+                h = linear_bias_act(h, w2, b2, act="none")
+            else:
+                h = F.linear(h, w2, b2)
             _rec.end("fc2_gemm", ev, (B * L * hid + hid * D + B * L * D) * e, 2 * B * L * D * hid)
             ev = _rec.begin()
             if next_windows is not None:

@@ -172,7 +172,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, q):
+def _nccl_worker(rank, world, port, q, precision="fp32"):
     import datetime
 
     import torch.distributed as dist
@@ -186,7 +186,7 @@ def _nccl_worker(rank, world, port, q):
 
         field_res, dim = (4, 36, 72), 128
         C, H, W = field_res
-        layer = _stage(dim, 2, 2, "fp32")
+        layer = _stage(dim, 2, 2, precision)
         g = torch.Generator().manual_seed(9)
         x = torch.randn(1, C * H * W, dim, generator=g).cuda()
         c = torch.randn(1, dim, generator=g).cuda()
@@ -204,13 +204,17 @@ def _nccl_worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_sharded_stage_nccl_two_gpus():
+@pytest.mark.parametrize("precision,tol", [("fp32", 1e-6), ("bf16_mixed", 5e-3)])
+def test_sharded_stage_nccl_two_gpus(precision, tol):
+    """Two ranks over NCCL (NVLS off): each band of the sharded stage against the same rows of the
+    unsharded stage. In bf16_mixed the forward halo travels in bf16; cuBLAS may pick another
+    algorithm for the band's row count, hence the bf16 tolerance."""
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q, precision)) for r in range(2)]
     for p in procs:
         p.start()
     out = {}
@@ -220,4 +224,4 @@ def test_sharded_stage_nccl_two_gpus():
     for p in procs:
         p.join(timeout=60)
     assert sorted(out) == [0, 1]
-    assert all(e <= 1e-6 for e in out.values()), out
+    assert all(e <= tol for e in out.values()), out
