@@ -106,12 +106,6 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, (kVec && kChunks <= 2) ? 
       wrow = b * (int64_t)a.wlp.nW * a.wlp.N + unmerge_slot(a.wlp, c, h, w);
     }
     float v[kChunks][kE];
-    // Rows of 256 and 1024 elements request their residual together with x, so that its DRAM
-    // latency overlaps the two reductions instead of following them (the warp's chain is
-    // latency-bound at the power-capped clock). At 512 elements the 64-register bound (four
-    // blocks per SM) would spill; at 2048 the registers would double and halve the occupancy.
-    constexpr bool kEarlyRes = kVec && (kChunks == 1 || kChunks == 4);
-    float rv[kEarlyRes ? kChunks : 1][8];
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < kChunks; ++i) {
@@ -119,9 +113,6 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, (kVec && kChunks <= 2) ? 
       if (col < D) {
         if constexpr (kVec) load8_any(xr + col, v[i], true);
         else v[i][0] = to_f32(xr[col]);
-        if constexpr (kEarlyRes) {
-          if (rg) Vec8<TO>::load_stream(rg + row * D + col, rv[i]);
-        }
       } else {
 #pragma unroll
         for (int e = 0; e < kE; ++e) v[i][e] = 0.f;
@@ -156,15 +147,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, (kVec && kChunks <= 2) ? 
 #pragma unroll
         for (int e = 0; e < 8; ++e) y[e] = (v[i][e] - mean) * rstd * (a.scale_bias + sc[e]) + sh[e];
         if (rg) {
-          if constexpr (kEarlyRes) {
+          float r[8];
+          Vec8<TO>::load_stream(rg + row * D + col, r);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) y[e] += rv[i][e];
-          } else {
-            float r[8];
-            Vec8<TO>::load_stream(rg + row * D + col, r);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) y[e] += r[e];
-          }
+          for (int e = 0; e < 8; ++e) y[e] += r[e];
         }
         Vec8<TO>::store(og + row * D + col, y);
         if (a.out_bf16) Vec8<__nv_bfloat16>::store(a.out_bf16 + row * D + col, y);
