@@ -31,7 +31,7 @@
 //                   deviations over the bf16 row in shared memory (two-pass variance, fp32).
 //               E2  warp = row: y = residual + (h - mean) * rstd * (scale_bias + scale) + shift,
 //                   coalesced 16-byte row I/O, four rows' residual loads in flight per warp; the
-//                   next tile's residual rows are prefetched into L2.
+//                   tile's residual rows are prefetched into L2 when its accumulator is ready.
 // The row statistics are summed in another order than the stand-alone AdaLN kernel's warp
 // reduction, so results agree with the unfused pair to fp32 rounding, not bit for bit.
 // Every mbarrier wait is bounded (status codes 18-23 in the GEMM status word).
@@ -259,6 +259,10 @@ gemm_adaln_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_con
       const bool ready = mbar_wait(BAR(kAccFull), (uint32_t)(j & 1), abort, p.status, 23, kTimeoutNs);
       if (!epi_all(ready)) break;
       tc_fence_after();
+      // This tile's residual rows start moving into L2 now, one E1 + E1b ahead of E2. A whole tile
+      // ahead was too early: the A stream of the next tile evicted them (ncu: the residual read
+      // twice from DRAM).
+      if (j > 0) prefetch_tile(j);
       // E1: accumulators + bias -> bf16 row tile, and this thread's half-row sum of the bf16 values.
       float acc4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
@@ -297,7 +301,6 @@ gemm_adaln_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_con
         else mbar_arrive_remote(map_shared_rank(BAR(kAccEmpty), 0));
       }
       epi_bar();  // every row of the h tile and every half-row sum is written
-      prefetch_tile(j + 1);
       // E1b (thread = row, the four half-0 warps): mean from the two half-row sums, then the sum
       // of squared deviations over the whole bf16 row from shared memory (two-pass variance).
       if (half == 0) {
