@@ -8,7 +8,8 @@
 //     tracked by mbarriers;
 //   * the consumer warps each own 16 query rows of the tile and run QK^T, the masked
 //     softmax (log2 domain, fp32) and PV on warp-level tensor-core MMAs reading the swizzled
-//     tiles with ldmatrix.
+//     tiles with ldmatrix (the mma.sync cross-check kernels; the production kernels below, tc
+//     and tc32, issue tcgen05 UMMAs into tensor memory instead).
 // FP32 I/O uses 3xTF32 (hi/lo split of both operands, three products), so it keeps fp32
 // accuracy, unlike the upstream 1xTF32 QK^T + BF16 PV kernel (ops/cute/_kernel_fp32.py:142).
 //
@@ -417,13 +418,13 @@ attn_sync_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
 //                  O  = P[0:128]  V   (M=128), O2 = P[80:144] V   (M=64)   (N=64, K=144, V MN-major)
 //                in whatever order their inputs become ready (non-blocking barrier tests),
 //                signalling completion with tcgen05.commit on mbarriers.
-//   warps 4..11  softmax + epilogue of rows 0..127: two warpgroups split every row, 72 key columns
-//                (and 32 output columns) each; the row max and row sum are exchanged through shared
-//                memory. S comes from TMEM (32x32b loads, one lane = one row per thread), P goes to
-//                shared memory as bf16 in the UMMA A-operand layout, O rows are scaled by 1/sum and
-//                written to global memory as bf16.
-//   warp 3       rows 128..143 from S2/O2 TMEM lanes 96..111 / 112..127 with 16x256b loads (16 rows spread
-//                over the 32 threads, two rows per thread, reductions over 4-thread quads).
+//   warps 3..11  softmax + epilogue, 16 query rows per warp: warps 4..11 take rows 0..127 of S / O
+//                (lanes 32*(w%4) + 16*((w-4)/4) .. +15 of the warp's TMEM quarter), warp 3 rows
+//                128..143 of S2 / O2 (lanes 96..111 / 112..127). All use 16x256b TMEM loads: a
+//                thread holds two rows x 36 keys, a row's 144 keys sit in four threads of one warp,
+//                so the row max and sum take two shuffles and no exchange between warps. P goes to
+//                shared memory as bf16 in the UMMA A-operand layout; O rows are scaled by 1/sum,
+//                staged in the tile's V slot and stored with one bulk tensor copy per tile.
 // The shifted-window mask (region ids) goes through the tensor cores: warp 0 writes, once per
 // window, one-hot region operands (32-byte swizzle) and the S UMMAs get one more K=16 step that
 // raises every same-region logit by 100/scale, which the softmax cannot tell from upstream's -100
@@ -444,12 +445,11 @@ constexpr int kPBytes = 2 * kPChunk + kRow32;
 // One-hot region operands of a window's mask UMMA (A: queries, B: keys), two windows in flight.
 constexpr int kMaskOpBytes = 2 * kRow32;
 constexpr int kMaskBytes = 2 * kMaskOpBytes;
-constexpr int kXchgBytes = 2 * 2 * 128 * 4;  // {max, sum} x warpgroup x row
 constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColS2 = 160, kColO0 = 320, kColO1 = 384, kColO2 = 448;
 constexpr int kNumBars = 34;
-constexpr int kSmem = kStages * kStageBytes + kPBytes + kMaskBytes + kXchgBytes + kNumBars * 8 + 16 + 16 + 1024;
+constexpr int kSmem = kStages * kStageBytes + kPBytes + kMaskBytes + kNumBars * 8 + 16 + 16 + 1024;
 static_assert(kSmem <= 227 * 1024, "shared memory budget");
 constexpr uint32_t kIdescS = ptx::make_idesc(1, 128, kMaxN, false, false);
 constexpr uint32_t kIdescO = ptx::make_idesc(1, 128, 64, false, true);
@@ -462,7 +462,7 @@ constexpr uint32_t kRowOff80_32 = 80 * 32;  // the same in a 32-byte-row tile (2
 constexpr uint32_t kLaneHalf = 16u << 16;
 
 enum { kFullQK = 0, kEmptyQK = 3, kFullV = 6, kEmptyV = 9, kSFull = 12, kSFree = 13, kPFull = 14, kPEmpty = 15,
-       kOFull = 16, kOFree = 18, kO2Full = 20, kO2Free = 22, kDone = 24, kXMax = 25, kXSum = 26,
+       kOFull = 16, kOFree = 18, kO2Full = 20, kO2Free = 22, kDone = 24,
        kMaskFull = 27, kMaskEmpty = 29, kOStaged = 31 };
 
 // Byte offset of bf16 element e (0..15) of row r in a 32-byte-swizzled K-major tile.
@@ -652,8 +652,7 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
   const uint32_t sbase = smem_u32(smem);
   const uint32_t sP = sbase + kStages * kStageBytes;
   const uint32_t sMask = sP + kPBytes;  // 256-byte aligned (32-byte-swizzle atoms)
-  float* xchg = reinterpret_cast<float*>(smem + kStages * kStageBytes + kPBytes + kMaskBytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kPBytes + kMaskBytes + kXchgBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kPBytes + kMaskBytes);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* mask_mode = reinterpret_cast<volatile int*>(tmem_holder + 4);  // per mask buffer
   const uint32_t bar0 = smem_u32(bars);
@@ -687,8 +686,6 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       mbar_init(BAR(kO2Free + b), 1);
     }
     mbar_init(BAR(kDone), 1);
-    mbar_init(BAR(kXMax), 8);  // row-max exchange between the two softmax warpgroups
-    mbar_init(BAR(kXSum), 8);  // row-sum exchange
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR(kMaskFull + b), 1);
       mbar_init(BAR(kMaskEmpty + b), 1);
@@ -917,148 +914,19 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       int no_abort = 0;
       mbar_wait(BAR(kDone), 0, &no_abort, p.status, 17, kTimeoutNs);
     }
-  } else if (warp >= 4) {
-    // ---------------- rows 0..127: softmax + epilogue, two warpgroups per row ----------------
-    const int g = (warp - 4) >> 2;  // key half: columns 72g .. 72g+71, output columns 32g .. 32g+31
-    const int q4 = warp & 3;
-    const int row = q4 * 32 + lane;
-    const uint32_t lane_addr = (uint32_t)(q4 * 32) << 16;
-    float* xmax = xchg;        // [2][128]
-    float* xsum = xchg + 256;  // [2][128]
-    int cached_w = -1, wseq = -1;
-    uint32_t rel[3] = {0u, 0u, 0u};
-    bool wmask = false;
-    float l_prev = 1.f;
-    int t_prev = -1, j_prev = -1;
-
-    auto epilogue = [&](int j, int t, float l) -> bool {
-      const int ob = j & 1;
-      if (!mbar_wait(BAR(kOFull + ob), (uint32_t)((j >> 1) & 1), abort, p.status, 19, kTimeoutNs)) return false;
-      tc_fence_after();
-      uint32_t o0[16], o1[16];
-      const uint32_t ta = tmem + lane_addr + (ob ? kColO1 : kColO0) + 32 * g;
-      tmem_ld16(ta, o0);
-      tmem_ld16(ta + 16, o1);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kOFree + ob));
-      // Stage the row (columns 32g .. 32g+31) in this tile's V slot, 128-byte swizzle; warp 2
-      // writes the whole tile with one bulk tensor store (rows past N are dropped by it).
-      (void)t;
-      const float inv = 1.f / l;
-      const float2 inv2 = make_float2(inv, inv);
-      uint32_t pk[16];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float2 y0 = __fmul2_rn(make_float2(__uint_as_float(o0[2 * e]), __uint_as_float(o0[2 * e + 1])), inv2);
-        const float2 y1 = __fmul2_rn(make_float2(__uint_as_float(o1[2 * e]), __uint_as_float(o1[2 * e + 1])), inv2);
-        pk[e] = pack_bf16x2(y0.x, y0.y);
-        pk[8 + e] = pack_bf16x2(y1.x, y1.y);
-      }
-      const uint32_t stg = sbase + (j % kStages) * kStageBytes + (uint32_t)kQKBytes + (uint32_t)row * 128u;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        st_shared_v4(stg + (uint32_t)((((4 * g + c) ^ (row & 7)) & 7) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
-                     pk[4 * c + 3]);
-      fence_proxy_async_shared();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kOStaged + j % kStages));
-      return true;
-    };
-
-    bool ok = true;
-    for (int i = 0; i < n_local; ++i) {
-      const int t = t_begin + i;
-      if constexpr (kBitsPath<kMask>) {  // per-logit masks only
-        const int w = t / p.H;
-        if (w != cached_w) {
-          cached_w = w;
-          ++wseq;
-          int mode = kModeBits;
-          if constexpr (kMask == kGroups) {
-            // The producer classified the window before its first load (mask buffer wseq & 1).
-            if (!mbar_wait(BAR(kMaskFull + (wseq & 1)), (uint32_t)((wseq >> 1) & 1), abort, p.status, 26,
-                           kTimeoutNs)) { ok = false; break; }
-            mode = mask_mode[wseq & 1];
-          }
-          uint32_t b[5] = {0u, 0u, 0u, 0u, 0u};
-          // Region masks of up to 16 regions are already in S (mask UMMA); others per logit.
-          if constexpr (kBitsPath<kMask>) {
-            if (mode == kModeBits) row_mask_bits<kMask>(p, w % p.nW, row, b);
-          }
-          wmask = (b[0] | b[1] | b[2] | b[3] | b[4]) != 0u;
-          // bits of keys 72g .. 72g+71
-          const uint32_t w0 = g ? b[2] : b[0], w1 = g ? b[3] : b[1], w2 = g ? b[4] : b[2];
-          const uint32_t w3 = g ? 0u : b[3];
-          const uint32_t sh = g ? 8u : 0u;
-          rel[0] = __funnelshift_r(w0, w1, sh);
-          rel[1] = __funnelshift_r(w1, w2, sh);
-          rel[2] = __funnelshift_r(w2, w3, sh) & 0xffu;
-        }
-      }
-      if (!mbar_wait(BAR(kSFull), (uint32_t)(i & 1), abort, p.status, 20, kTimeoutNs)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t v[72];
-      tmem_ld72(tmem + lane_addr + kColS + 72 * g, v);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kSFree));
-      float pm;
-      if (kBitsPath<kMask> && wmask) pm = raw_logits72<kBitsPath<kMask>, kFullN>(v, rel, braw, 72 * g, p.N);
-      else pm = raw_logits72<false, kFullN>(v, rel, braw, 72 * g, p.N);
-      // Each slot is rewritten only after the partner passed the other exchange barrier of the
-      // same tile, so one slot per value suffices.
-      xmax[g * 128 + row] = pm;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kXMax));
-      if (!mbar_wait(BAR(kXMax), (uint32_t)(i & 1), abort, p.status, 24, kTimeoutNs)) { ok = false; break; }
-      const float m = fmaxf(pm, xmax[(g ^ 1) * 128 + row]);
-      const float c = p.scale_log2, mc = -m * c;
-      // Paired fp32 FMAs and adds (two logits per instruction; each element's value is the same
-      // as with scalar fmaf).
-      const float2 c2 = make_float2(c, c), mc2 = make_float2(mc, mc);
-      uint32_t pk[36];
-      float2 l2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#pragma unroll
-      for (int k = 0; k < 72; k += 2) {
-        const float2 y = __ffma2_rn(make_float2(__uint_as_float(v[k]), __uint_as_float(v[k + 1])), c2, mc2);
-        const float a = ex2(y.x), b = ex2(y.y);
-        l2[(k >> 1) & 1] = __fadd2_rn(l2[(k >> 1) & 1], make_float2(a, b));
-        pk[k >> 1] = pack_bf16x2(a, b);
-      }
-      const float pl = (l2[0].x + l2[0].y) + (l2[1].x + l2[1].y);
-      // The row sum is only needed by the epilogue (1/l): publish this half's sum now and collect
-      // the partner's after P is handed to the tensor cores, off the path to the PV UMMAs.
-      xsum[g * 128 + row] = pl;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kXSum));
-      if (!mbar_wait(BAR(kPEmpty), (uint32_t)((i & 1) ^ 1), abort, p.status, 21, kTimeoutNs)) { ok = false; break; }
-#pragma unroll
-      for (int jj = 0; jj < 9; ++jj) {
-        const int j16 = 9 * g + jj;  // 8-key group 0..17
-        const uint32_t addr = j16 < 16 ? sP + (j16 >> 3) * kPChunk + row * 128 + (((j16 & 7) ^ (row & 7)) << 4)
-                                       : sP + 2 * kPChunk + sw32_offset(row, (j16 & 1) * 8);
-        st_shared_v4(addr, pk[4 * jj], pk[4 * jj + 1], pk[4 * jj + 2], pk[4 * jj + 3]);
-      }
-      fence_proxy_async_shared();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kPFull));
-      // The partner reads this slot before it arrives at the next tile's max exchange, which this
-      // warpgroup waits for before writing the slot again.
-      if (!mbar_wait(BAR(kXSum), (uint32_t)(i & 1), abort, p.status, 25, kTimeoutNs)) { ok = false; break; }
-      const float l = pl + xsum[(g ^ 1) * 128 + row];
-      if (j_prev >= 0 && !epilogue(j_prev, t_prev, l_prev)) { ok = false; break; }
-      j_prev = i;
-      t_prev = t;
-      l_prev = l;
-    }
-    if (ok && j_prev >= 0) epilogue(j_prev, t_prev, l_prev);
-  } else if (warp == 3) {
-    // ---------------- rows 128..143 (S2/O2 lanes 112..127, 16x256b) ----------------
+  } else {
+    // ---------------- softmax + output rows, 16 rows per warp (16x256b TMEM loads) ----------------
+    // Warps 4..11 take rows 0..127 of the M=128 S and O accumulators: warp w reads lanes
+    // 32*(w%4) + 16*((w-4)/4) .. +15 of its TMEM quarter. Warp 3 takes rows 128..143 from the M=64
+    // S2 / O2 blocks over rows 80..143 (A rows 48..63 land in lanes 96..111). A thread holds rows
+    // ra = base + lane/4 and rb = ra + 8, 36 keys each; a row's 144 keys sit in 4 threads of one
+    // warp, so its max and sum take two shuffles and no exchange between warps.
+    const bool rem = warp == 3;
     const int t0 = lane & 3, t1 = lane >> 2;
-    const int ra = 128 + t1, rb = 136 + t1;
-    const uint32_t lane_addr = 96u << 16;  // A rows 48..63 of the M=64 blocks
+    const int rbase = rem ? 128 : 32 * (warp & 3) + 16 * ((warp - 4) >> 2);
+    const int ra = rbase + t1, rb = rbase + 8 + t1;
+    const uint32_t lane_addr = rem ? (96u << 16) : ((uint32_t)rbase << 16);
+    const uint32_t s_col = rem ? kColS2 : kColS;
     int cached_w = -1, wseq = -1;
     uint32_t ta = 0, tb = 0, kp[18];
     bool wmask = false;
@@ -1069,15 +937,19 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
 
     auto epilogue_rem = [&](int j, int t, float la, float lb) -> bool {
       const int ob = j & 1;
-      if (!mbar_wait(BAR(kO2Full + ob), (uint32_t)((j >> 1) & 1), abort, p.status, 23, kTimeoutNs)) return false;
+      if (!mbar_wait(BAR((rem ? kO2Full : kOFull) + ob), (uint32_t)((j >> 1) & 1), abort, p.status, rem ? 23 : 19,
+                     kTimeoutNs))
+        return false;
       tc_fence_after();
       uint32_t o[32];
-      tmem_ld_16x256b_r32(tmem + lane_addr + kColO2 + (ob ? kLaneHalf : 0u), o);
+      const uint32_t o_col = rem ? kColO2 + (ob ? kLaneHalf : 0u) : (ob ? kColO1 : kColO0);
+      tmem_ld_16x256b_r32(tmem + lane_addr + o_col, o);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(kO2Free + ob));
-      // Rows 128..143 of the tile's staged output (see the softmax epilogue).
+      if (lane == 0) mbar_arrive(BAR((rem ? kO2Free : kOFree) + ob));
+      // Rows ra, rb of the tile's output, O / l in bf16, staged in the tile's V slot (128-byte
+      // swizzle); warp 2 writes the whole tile with one bulk tensor store (rows past N dropped).
       (void)t;
       const float ia = 1.f / la, ib = 1.f / lb;
       const float2 ia2 = make_float2(ia, ia), ib2 = make_float2(ib, ib);
@@ -1141,8 +1013,8 @@ attn_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_consta
       uint32_t v[72];
       {
         uint32_t a[64], b[8];
-        tmem_ld_16x256b_r64(tmem + lane_addr + kColS2, a);
-        tmem_ld_16x256b_r8(tmem + lane_addr + kColS2 + 128, b);
+        tmem_ld_16x256b_r64(tmem + lane_addr + s_col, a);
+        tmem_ld_16x256b_r8(tmem + lane_addr + s_col + 128, b);
         tmem_wait_ld();
 #pragma unroll
         for (int k = 0; k < 64; ++k) v[k] = a[k];
