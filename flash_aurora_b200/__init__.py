@@ -22,6 +22,7 @@ from .linear import linear_bias_act
 from .perceiver_ln import layernorm_affine_add_residual_forward, layernorm_affine_forward
 from .adaln import (
     adaptive_layernorm_film_add_residual_forward,
+    adaptive_layernorm_film_add_residual_rows,
     adaptive_layernorm_film_forward,
     unmerge_adaptive_layernorm_film_add_residual,
     unmerge_adaptive_layernorm_film_add_residual_band,
@@ -60,6 +61,7 @@ __all__ = [
     "layernorm_affine_forward",
     "layernorm_affine_add_residual_forward",
     "adaptive_layernorm_film_add_residual_forward",
+    "adaptive_layernorm_film_add_residual_rows",
     "adaptive_layernorm_film_forward",
     "unmerge_adaptive_layernorm_film_add_residual",
     "unmerge_adaptive_layernorm_film_add_residual_band",

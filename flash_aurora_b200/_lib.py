@@ -50,7 +50,9 @@ SIGNATURES = {
     "fa_crop_roll_unmerge_band": (_i32, [_vp, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64,
                                          _i32p, _i32p, _vp]),
     "fa_unmerge_adaln_film_band": (_i32, [_vp, _vp, _i32, _vp, _i32, _vp, _vp, _i32, _f32, _f32, _vp, _i32, _vp,
-                                          _i64, _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _vp]),
+                                          _i64, _i64, _i64, _i64, _i64, _i64, _i32p, _i32p, _i64, _i64, _vp]),
+    "fa_adaln_film_rows": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _f32, _f32, _vp, _i32, _vp, _i64, _i64, _i64,
+                                  _i64, _i64, _i64, _i64, _vp]),
     "fa_linear_bias_act": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
     "fa_gemm_status": (_i32, [ctypes.POINTER(ctypes.c_int)]),
     "fa_gemm_status_reset": (_i32, [_vp]),

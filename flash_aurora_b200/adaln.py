@@ -22,6 +22,7 @@ __all__ = [
     "unmerge_adaptive_layernorm_film_add_residual",
     "unmerge_adaptive_layernorm_film_add_residual_band",
     "adaptive_layernorm_film_add_residual_partition",
+    "adaptive_layernorm_film_add_residual_rows",
 ]
 
 _MAX_D = 2048
@@ -118,6 +119,54 @@ def adaptive_layernorm_film_add_residual_forward(
     return out
 
 
+def adaptive_layernorm_film_add_residual_rows(
+    residual: torch.Tensor,
+    x: torch.Tensor,
+    scale: torch.Tensor,
+    shift: torch.Tensor,
+    res: tuple[int, int, int],
+    rows: tuple[int, int],
+    scale_bias: float,
+    eps: float = 1e-5,
+    *,
+    out: torch.Tensor,
+    out_bf16: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """:func:`adaptive_layernorm_film_add_residual_forward` (fp32 output) on the token rows
+    ``(b, c, h, w)`` of the ``res = (C, H, W)`` grid with ``h`` in ``[rows[0], rows[0] + rows[1])``,
+    written into ``out``; other rows of ``out`` are untouched. Two calls over complementary row
+    ranges equal one full call."""
+    for t in (residual, x, out):
+        _lib.require_cuda(t, "adaptive_layernorm_film_add_residual_rows")
+    if residual.dtype != torch.float32 or x.dtype not in _DTYPES:
+        raise ValueError("residual must be float32 and x float32/bfloat16")
+    if residual.shape != x.shape:
+        raise ValueError("residual and x must have the same shape.")
+    C, H, W = (int(v) for v in res)
+    B, L, D = x.shape
+    if L != C * H * W:
+        raise ValueError(f"x has {L} tokens, res {tuple(res)} has {C * H * W}")
+    if D > _MAX_D:
+        raise ValueError(f"AdaLN supports D <= {_MAX_D}")
+    h0, hn = int(rows[0]), int(rows[1])
+    if h0 < 0 or hn < 0 or h0 + hn > H:
+        raise ValueError(f"rows {rows} outside the grid's {H} rows")
+    if (tuple(out.shape) != (B, L, D) or out.dtype != torch.float32 or not out.is_contiguous()
+            or out.device != x.device):
+        raise ValueError(f"out must be a contiguous float32 tensor of shape {(B, L, D)} on {x.device}")
+    _check_out_bf16(out_bf16, B, L, D, x.device)
+    scale = _mod_rows(scale, B, D, "scale")
+    shift = _mod_rows(shift, B, D, "shift").to(scale.dtype)
+    x, residual = x.contiguous(), residual.contiguous()
+    rc = _lib.load().fa_adaln_film_rows(
+        x.data_ptr(), _lib.dtype_code(x.dtype), residual.data_ptr(), _lib.FA_F32, scale.data_ptr(),
+        shift.data_ptr(), _lib.dtype_code(scale.dtype), float(scale_bias), float(eps), out.data_ptr(),
+        _lib.FA_F32, out_bf16.data_ptr() if out_bf16 is not None else None, B, C, H, W, D, h0, hn,
+        _lib.stream_ptr(x.device))
+    _lib.check(rc, "adaptive_layernorm_film_add_residual_rows")
+    return out
+
+
 def unmerge_adaptive_layernorm_film_add_residual(
     windows: torch.Tensor,
     residual: torch.Tensor,
@@ -176,10 +225,16 @@ def unmerge_adaptive_layernorm_film_add_residual_band(
     eps: float = 1e-5,
     *,
     out_bf16: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
+    rows: Optional[tuple[int, int]] = None,
 ) -> torch.Tensor:
     """Latitude-band form of :func:`unmerge_adaptive_layernorm_film_add_residual`: the band's first
     ``s = shift_h`` rows are read from ``halo_in (B, C, s, W, D)``, the previous band's halo
-    extract (same dtype as ``windows``)."""
+    extract (same dtype as ``windows``).
+
+    ``rows = (h_begin, h_count)`` writes only those band rows of ``out`` (and ``out_bf16``);
+    ``halo_in`` may then be ``None`` when ``h_begin >= s``. Used to normalise the rows that need
+    no halo while the halo is in flight."""
     _lib.require_cuda(windows, "unmerge_adaptive_layernorm_film_add_residual_band")
     _lib.require_cuda(residual, "unmerge_adaptive_layernorm_film_add_residual_band")
     if windows.dtype not in _DTYPES or residual.dtype != torch.float32:
@@ -193,9 +248,13 @@ def unmerge_adaptive_layernorm_film_add_residual_band(
     ws, ss, nW, N = band_geometry(band_res, field_res, window_size, shift_size)
     if tuple(windows.shape) != (B * nW, N, D):
         raise ValueError(f"windows must have shape {(B * nW, N, D)}, got {tuple(windows.shape)}")
-    if ss[1]:
+    h0, hn = (0, Hb) if rows is None else (int(rows[0]), int(rows[1]))
+    if h0 < 0 or hn < 0 or h0 + hn > Hb:
+        raise ValueError(f"rows {rows} outside the band's {Hb} rows")
+    if ss[1] and h0 < ss[1] and hn > 0:
         if halo_in is None:
             raise ValueError(f"a band with an H shift of {ss[1]} rows needs halo_in")
+    if ss[1] and halo_in is not None:
         if tuple(halo_in.shape) != (B, C, ss[1], W, D) or halo_in.dtype != windows.dtype:
             raise ValueError(f"halo_in must be {windows.dtype} of shape {(B, C, ss[1], W, D)}")
         _lib.require_cuda(halo_in, "unmerge_adaptive_layernorm_film_add_residual_band")
@@ -206,13 +265,17 @@ def unmerge_adaptive_layernorm_film_add_residual_band(
     scale = _mod_rows(scale, B, D, "scale")
     shift = _mod_rows(shift, B, D, "shift").to(scale.dtype)
     windows, residual = windows.contiguous(), residual.contiguous()
-    out = torch.empty(B, L, D, device=residual.device, dtype=torch.float32)
+    if out is None:
+        out = torch.empty(B, L, D, device=residual.device, dtype=torch.float32)
+    elif (tuple(out.shape) != (B, L, D) or out.dtype != torch.float32 or not out.is_contiguous()
+          or out.device != residual.device):
+        raise ValueError(f"out must be a contiguous float32 tensor of shape {(B, L, D)} on {residual.device}")
     rc = _lib.load().fa_unmerge_adaln_film_band(
         windows.data_ptr(), halo_in.data_ptr() if halo_in is not None else None, _lib.dtype_code(windows.dtype),
         residual.data_ptr(), _lib.FA_F32, scale.data_ptr(), shift.data_ptr(), _lib.dtype_code(scale.dtype),
         float(scale_bias), float(eps), out.data_ptr(), _lib.FA_F32,
         out_bf16.data_ptr() if out_bf16 is not None else None, B, C, Hb, field_res[1], W, D,
-        _lib.i32x3(window_size), _lib.i32x3(shift_size), _lib.stream_ptr(residual.device))
+        _lib.i32x3(window_size), _lib.i32x3(shift_size), h0, hn, _lib.stream_ptr(residual.device))
     _lib.check(rc, "unmerge_adaptive_layernorm_film_add_residual_band")
     return out
 

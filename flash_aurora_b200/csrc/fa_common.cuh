@@ -50,6 +50,34 @@ int make_geometry(int64_t C, int64_t H, int64_t W, const int32_t* window_size,
 int make_band_geometry(int64_t C, int64_t H_band, int64_t H_field, int64_t W,
                        const int32_t* window_size, const int32_t* shift_size, Geometry* g);
 
+// ---------------------------------------------------------------------------------------------
+// Division of a non-negative 31-bit integer n by a run-time divisor d (1 <= d < 2^31) with one
+// 32 x 32 -> 64-bit multiply and a shift, after Granlund & Montgomery, "Division by invariant
+// integers using multiplication" (PLDI 1994): with l = ceil(log2 d), p = 31 + l and
+// m = ceil(2^p / d) (< 2^32), m * d = 2^p + e with 0 <= e < d <= 2^l, so
+// n * m / 2^p = n / d + n * e / (d * 2^p) and the second term is below 2^-l <= 1 / d: the floor
+// is floor(n / d). The index maps of the gathers divide by window and grid extents per row, which
+// the hardware's integer division would otherwise spend tens of instructions on each.
+// ---------------------------------------------------------------------------------------------
+struct FastDiv {
+  uint32_t d, m, p;
+};
+
+inline FastDiv make_fastdiv(int64_t d) {
+  FastDiv f;
+  f.d = (uint32_t)(d < 1 ? 1 : d);
+  uint32_t l = 0;
+  while ((1ull << l) < f.d) ++l;
+  f.p = 31 + l;
+  f.m = (uint32_t)(((1ull << f.p) + f.d - 1) / f.d);
+  return f;
+}
+
+// floor(n / f.d) for 0 <= n < 2^31.
+__host__ __device__ __forceinline__ int32_t fdiv(int32_t n, const FastDiv& f) {
+  return (int32_t)(((uint64_t)(uint32_t)n * f.m) >> f.p);
+}
+
 // Device-side copy of the index parameters of a layout gather.
 struct LayoutParams {
   int32_t C, H, W;
@@ -65,7 +93,20 @@ struct LayoutParams {
   int32_t band;
   int32_t Hout;  // rows of an unmerge output grid: H, or `band` for the halo extract
   int32_t hs0;   // band mode: shifted row of unmerge output row 0 (-band, or H - band)
+  // Divisors of the index maps (see FastDiv).
+  FastDiv f_W, f_Hout, f_wc, f_wh, f_ww, f_W1, f_HW1, f_whw;
 };
+
+inline void set_divisors(LayoutParams& p) {
+  p.f_W = make_fastdiv(p.W);
+  p.f_Hout = make_fastdiv(p.Hout);
+  p.f_wc = make_fastdiv(p.wc);
+  p.f_wh = make_fastdiv(p.wh);
+  p.f_ww = make_fastdiv(p.ww);
+  p.f_W1 = make_fastdiv(p.W1);
+  p.f_HW1 = make_fastdiv(p.HW1);
+  p.f_whw = make_fastdiv((int64_t)p.wh * p.ww);
+}
 
 inline LayoutParams layout_params(const Geometry& g) {
   LayoutParams p;
@@ -80,6 +121,7 @@ inline LayoutParams layout_params(const Geometry& g) {
   p.band = 0;
   p.Hout = p.H;
   p.hs0 = 0;
+  set_divisors(p);
   return p;
 }
 
@@ -92,21 +134,31 @@ inline LayoutParams band_layout_params(const Geometry& g, bool extract) {
   p.sh = 0;
   p.Hout = extract ? p.band : p.H;
   p.hs0 = extract ? p.H - p.band : -p.band;
+  set_divisors(p);
   return p;
+}
+
+// Token (c, h, w) of token index t < C * Hout * W of the unmerge output grid.
+__device__ __forceinline__ void unmerge_token(const LayoutParams& p, int32_t t, int32_t& c, int32_t& h,
+                                              int32_t& w) {
+  const int32_t q = fdiv(t, p.f_W);
+  w = t - q * p.W;
+  c = fdiv(q, p.f_Hout);
+  h = q - c * p.Hout;
 }
 
 // Source token (c*H + h)*W + w of window slot (win, n) of one batch element, or -1 for pad.
 // Same mapping as ops/triton_swin3d_layout.py:218-246. In band mode a result >= C*H*W is
 // halo token (result - C*H*W) of layout (C, band, W).
 __device__ __forceinline__ int32_t partition_source(const LayoutParams& p, int32_t win, int32_t n) {
-  const int32_t c1 = win / p.HW1;
+  const int32_t c1 = fdiv(win, p.f_HW1);
   const int32_t r1 = win - c1 * p.HW1;
-  const int32_t h1 = r1 / p.W1;
+  const int32_t h1 = fdiv(r1, p.f_W1);
   const int32_t w1 = r1 - h1 * p.W1;
   const int32_t whw = p.wh * p.ww;
-  const int32_t wc = n / whw;
+  const int32_t wc = fdiv(n, p.f_whw);
   const int32_t r2 = n - wc * whw;
-  const int32_t wh = r2 / p.ww;
+  const int32_t wh = fdiv(r2, p.f_ww);
   const int32_t ww = r2 - wh * p.ww;
   const int32_t cs = c1 * p.wc + wc - p.pc;
   const int32_t hs = h1 * p.wh + wh - p.ph;
@@ -141,9 +193,9 @@ __device__ __forceinline__ int32_t unmerge_slot(const LayoutParams& p, int32_t c
   }
   int32_t wsv = w - p.sw; if (wsv < 0) wsv += p.W;
   const int32_t pc = cs + p.pc, ph = hs + p.ph, pw = wsv + p.pw;
-  const int32_t c1 = pc / p.wc, wc = pc - c1 * p.wc;
-  const int32_t h1 = ph / p.wh, wh = ph - h1 * p.wh;
-  const int32_t w1 = pw / p.ww, ww = pw - w1 * p.ww;
+  const int32_t c1 = fdiv(pc, p.f_wc), wc = pc - c1 * p.wc;
+  const int32_t h1 = fdiv(ph, p.f_wh), wh = ph - h1 * p.wh;
+  const int32_t w1 = fdiv(pw, p.f_ww), ww = pw - w1 * p.ww;
   const int32_t win = c1 * p.HW1 + h1 * p.W1 + w1;
   const int32_t n = (wc * p.wh + wh) * p.ww + ww;
   return win * p.N + n;

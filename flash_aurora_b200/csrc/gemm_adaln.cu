@@ -349,9 +349,8 @@ gemm_adaln_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_con
           if constexpr (kMode == kRowsTokens) {
             if (p.win_out) {
               const int32_t t = (int32_t)(tok[k] - (int64_t)bb[k] * p.L);
-              const int32_t w = t % p.wlp.W;
-              const int32_t hh = (t / p.wlp.W) % p.wlp.H;
-              const int32_t cc = t / (p.wlp.W * p.wlp.H);
+              int32_t cc, hh, w;
+              unmerge_token(p.wlp, t, cc, hh, w);
               wrow = bb[k] * (int64_t)p.wlp.nW * p.wlp.N + unmerge_slot(p.wlp, cc, hh, w);
             }
           }

@@ -82,9 +82,8 @@ unmerge_kernel(const TIn* __restrict__ win, const TIn* __restrict__ halo_in, TOu
        row += (int64_t)gridDim.x * kWarpsPerBlock) {
     const int64_t b = row / tokens;
     const int32_t t = (int32_t)(row - b * tokens);
-    const int32_t w = t % p.W;
-    const int32_t h = (t / p.W) % p.Hout;
-    const int32_t c = t / (p.W * p.Hout);
+    int32_t c, h, w;
+    unmerge_token(p, t, c, h, w);
     const int32_t slot = unmerge_slot(p, c, h, w);
     // Band mode: the first `band` rows come from the previous band's halo-back rows.
     const TIn* s = slot >= 0 ? win + (b * (int64_t)p.nW * p.N + slot) * D

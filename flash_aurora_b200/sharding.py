@@ -29,6 +29,7 @@ deadline. On expiry the process group is aborted (which ends NCCL's spinning tra
 
 from __future__ import annotations
 
+import os
 import time
 from dataclasses import dataclass, field
 from datetime import timedelta
@@ -40,6 +41,8 @@ from .util import maybe_adjust_windows
 
 __all__ = [
     "HaloExchangeError",
+    "HaloHandle",
+    "halo_process_group",
     "band_bounds",
     "BandContext",
     "LocalRing",
@@ -48,6 +51,19 @@ __all__ = [
 
 class HaloExchangeError(RuntimeError):
     """A halo exchange with a neighbouring band did not complete."""
+
+
+def halo_process_group(timeout_s: float = 60.0):
+    """A NCCL process group over all ranks for the halo exchanges, whose internal streams have
+    high priority: an exchange issued while a large kernel occupies the GPU gets its SMs as soon
+    as blocks of that kernel retire, instead of after the whole kernel. A collective call: every
+    rank calls it once, in the same order relative to its other group creations."""
+    import torch.distributed as dist
+
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.is_high_priority_stream = True
+    return dist.new_group(ranks=list(range(dist.get_world_size())), backend="nccl", pg_options=opts,
+                          timeout=timedelta(seconds=timeout_s))
 
 
 def band_bounds(field_res, window_size, world: int) -> list[tuple[int, int]]:
@@ -108,7 +124,8 @@ class BandContext:
     """
 
     def __init__(self, field_res, window_size, rank: int, world: int, *, group=None,
-                 ring: Optional[LocalRing] = None, timeout_s: float = 60.0) -> None:
+                 ring: Optional[LocalRing] = None, timeout_s: float = 60.0,
+                 overlap: Optional[bool] = None) -> None:
         self.field_res = tuple(int(v) for v in field_res)
         self.window_size = tuple(int(v) for v in window_size)
         self.rank, self.world = int(rank), int(world)
@@ -119,12 +136,20 @@ class BandContext:
         self.group = group
         self.ring = ring
         self.timeout_s = float(timeout_s)
+        # Overlap the halo exchanges with the rows that do not need them (default; the
+        # FA_BAND_OVERLAP=0 environment setting or overlap=False exchange in line instead).
+        if overlap is None:
+            overlap = os.environ.get("FA_BAND_OVERLAP", "1") != "0"
+        self.overlap = bool(overlap)
         self.prev = (self.rank - 1) % self.world
         self.next = (self.rank + 1) % self.world
         self._gids: dict = {}
         self._bufs: dict = {}
         # Unfinished NCCL exchanges: (event after the transfers, host time issued, dst, src).
         self._pending: list = []
+        self._streams: dict = {}
+        # Forward halo issued by the previous block for the next shifted block: (key, handle).
+        self._fwd_prefetch = None
 
     # ------------------------------------------------------------------ geometry
     @property
@@ -207,6 +232,45 @@ class BandContext:
             raise HaloExchangeError(
                 f"rank {self.rank}: halo exchange (send to {dst}, receive from {src}) failed: {e}") from e
 
+    def _overlapped(self, t: torch.Tensor) -> bool:
+        """Exchanges of ``t`` run on a side stream: NCCL between processes only (gloo and the
+        thread ring exchange on the host, a single band copies locally)."""
+        return t.is_cuda and self.world > 1 and self.ring is None
+
+    def comm_stream(self, device) -> "torch.cuda.Stream":
+        """The side stream that overlapped exchanges (and their staging copies) run on."""
+        key = str(device)
+        st = self._streams.get(key)
+        if st is None:
+            st = torch.cuda.Stream(device=device, priority=-1)  # high priority, like the NCCL streams
+            self._streams[key] = st
+        return st
+
+    def exchange_async(self, send: torch.Tensor, recv: torch.Tensor, dst: int, src: int,
+                       stage: Optional[Callable[[], None]] = None) -> "HaloHandle":
+        """:meth:`exchange` ordered after the current stream's work so far but run on the side
+        stream, so the current stream can go on with work that does not need ``recv``; the
+        returned handle's :meth:`HaloHandle.wait` orders the current stream after the transfer.
+        ``stage`` (optional) fills ``send`` first, on the side stream. Without a side stream
+        (gloo, the thread ring, one band) the exchange completes before this returns."""
+        if not self._overlapped(recv):
+            if stage is not None:
+                stage()
+            self.exchange(send, recv, dst, src)
+            return HaloHandle(recv, None)
+        cur = torch.cuda.current_stream(recv.device)
+        comm = self.comm_stream(recv.device)
+        ready = torch.cuda.Event()
+        ready.record(cur)
+        with torch.cuda.stream(comm):
+            comm.wait_event(ready)
+            if stage is not None:
+                stage()
+            self.exchange(send, recv, dst, src)
+            done = torch.cuda.Event()
+            done.record(comm)
+        return HaloHandle(recv, done)
+
     def _check_pending(self, block: bool) -> None:
         """Drop finished exchanges; raise when the oldest unfinished one is past the deadline.
         With ``block`` poll until every pending exchange finished or the deadline passed."""
@@ -245,22 +309,60 @@ class BandContext:
     def halo_forward(self, x_band: torch.Tensor, s: int, dtype: Optional[torch.dtype] = None) -> torch.Tensor:
         """Receive the next band's first ``s`` rows: ``x_band (B, C, Hb, W, D)`` -> ``(B, C, s, W, D)``.
 
-        This rank sends its own first ``s`` rows to the previous band at the same time.
+        This rank sends its own first ``s`` rows to the previous band at the same time. When the
+        block that produced ``x_band`` already issued that exchange (:meth:`prefetch_forward_halo`)
+        the current stream only waits for it.
         """
         B, C, _, W, D = x_band.shape
         dtype = x_band.dtype if dtype is None else dtype
+        key = (x_band.data_ptr(), tuple(x_band.shape), int(s), dtype)
+        pre, self._fwd_prefetch = self._fwd_prefetch, None
+        if pre is not None:
+            if pre[0] != key:
+                raise RuntimeError("the prefetched forward halo was issued for another tensor or shift")
+            return pre[1].wait()
+        return self.prefetch_forward_halo(x_band, s, dtype, _keep=False).wait()
+
+    def prefetch_forward_halo(self, x_band: torch.Tensor, s: int, dtype: Optional[torch.dtype] = None, *,
+                              _keep: bool = True) -> "HaloHandle":
+        """Issue the forward-halo exchange of ``x_band`` now, as soon as its first ``s`` rows are
+        written, so that it overlaps the rest of the producing block; the next shifted block's
+        :meth:`halo_forward` of the same tensor waits for it. Every rank must prefetch for the same
+        blocks (the exchanges pair up in issue order)."""
+        B, C, _, W, D = x_band.shape
+        dtype = x_band.dtype if dtype is None else dtype
         send = self.buffer("fwd_send", (B, C, s, W, D), dtype, x_band.device)
-        send.copy_(x_band[:, :, :s])
         recv = self.buffer("fwd_recv", (B, C, s, W, D), dtype, x_band.device)
-        self.exchange(send, recv, dst=self.prev, src=self.next)
-        return recv
+        handle = self.exchange_async(send, recv, dst=self.prev, src=self.next,
+                                     stage=lambda: send.copy_(x_band[:, :, :s]))
+        if _keep:
+            self._fwd_prefetch = ((x_band.data_ptr(), tuple(x_band.shape), int(s), dtype), handle)
+        return handle
 
     def halo_back(self, rows: torch.Tensor) -> torch.Tensor:
         """Send the halo-back rows ``(B, C, s, W, D)`` to the next band; receive this band's own
         first ``s`` rows, computed by the previous band."""
+        return self.halo_back_async(rows).wait()
+
+    def halo_back_async(self, rows: torch.Tensor) -> "HaloHandle":
+        """:meth:`halo_back` on the side stream: the caller normalises the band rows that need
+        no halo meanwhile and waits on the handle before the first ``s`` rows."""
         recv = self.buffer("back_recv", tuple(rows.shape), rows.dtype, rows.device)
-        self.exchange(rows, recv, dst=self.next, src=self.prev)
-        return recv
+        return self.exchange_async(rows, recv, dst=self.next, src=self.prev)
+
+
+class HaloHandle:
+    """A halo exchange in flight: :meth:`wait` orders the current stream after the transfer and
+    returns the receive buffer."""
+
+    def __init__(self, recv: torch.Tensor, done: Optional["torch.cuda.Event"]) -> None:
+        self.recv = recv
+        self.done = done
+
+    def wait(self) -> torch.Tensor:
+        if self.done is not None:
+            torch.cuda.current_stream(self.recv.device).wait_event(self.done)
+        return self.recv
 
 
 def run_ranks(world: int, fn: Callable[[int, LocalRing], object], timeout_s: float = 120.0) -> list:

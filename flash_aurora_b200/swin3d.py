@@ -44,6 +44,7 @@ from .adaln import (
     adaptive_layernorm_film_add_residual_partition,
     unmerge_adaptive_layernorm_film_add_residual,
     unmerge_adaptive_layernorm_film_add_residual_band,
+    adaptive_layernorm_film_add_residual_rows,
 )
 from . import _lib
 from . import recorder as _rec
@@ -204,7 +205,8 @@ class Swin3DTransformerBlock(nn.Module):
                 warped: bool = True, band: Optional[BandContext] = None,
                 windows: Optional[torch.Tensor] = None,
                 next_windows: Optional[tuple] = None,
-                mods: Optional[tuple] = None) -> torch.Tensor:
+                mods: Optional[tuple] = None,
+                halo_prefetch: Optional[int] = None) -> torch.Tensor:
         """``x (B, C*H*W, D)`` fp32, ``c (B, ctx)`` -> ``(B, C*H*W, D)`` fp32.
 
         With ``band`` (a :class:`~flash_aurora_b200.sharding.BandContext`), ``x`` and ``res`` are
@@ -219,6 +221,10 @@ class Swin3DTransformerBlock(nn.Module):
         norm2 (the partition is then skipped). ``next_windows = (shift_size, buffer)``: also write
         the output into ``buffer`` in the window layout of a following block with that shift
         (same window size); ``buffer`` keeps zeros in its pad slots.
+
+        ``halo_prefetch = s`` (with ``band``): the next block is shifted by ``s`` rows. Its forward
+        halo (the first ``s`` rows of this block's output) is normalised first and handed to the
+        band's side stream while the other rows are normalised.
         """
         if not x.is_cuda:
             raise RuntimeError("Swin3DTransformerBlock.forward requires CUDA tensors (no CPU path).")
@@ -230,6 +236,8 @@ class Swin3DTransformerBlock(nn.Module):
         x = x.contiguous()
         if band is not None and tuple(res) != band.res:
             raise ValueError(f"res {tuple(res)} is not the band's resolution {band.res}")
+        if halo_prefetch and (band is None or not 0 < halo_prefetch < H):
+            raise ValueError("halo_prefetch needs a band taller than the halo")
         field_res = band.field_res if band is not None else tuple(res)
         ws, ss = maybe_adjust_windows(self.window_size, self.shift_size, field_res)
         if band is not None:
@@ -298,7 +306,7 @@ class Swin3DTransformerBlock(nn.Module):
                 x1 = unmerge_adaptive_layernorm_film_add_residual(
                     a, x, sc1, sh1, res, self.window_size, self.shift_size, float(self.norm1.scale_bias), eps,
                     out_bf16=x1_bf16)
-            else:
+            elif not ss[1] or not band.overlap:
                 halo_in = None
                 if ss[1]:
                     rows = band_halo_extract(a, res, field_res, self.window_size, self.shift_size,
@@ -307,6 +315,19 @@ class Swin3DTransformerBlock(nn.Module):
                 x1 = unmerge_adaptive_layernorm_film_add_residual_band(
                     a, halo_in, x, sc1, sh1, res, field_res, self.window_size, self.shift_size,
                     float(self.norm1.scale_bias), eps, out_bf16=x1_bf16)
+            else:
+                # The band's last s shifted rows go to the next band while the rows that need no
+                # halo are normalised; the first s rows wait for the previous band's rows.
+                s1 = ss[1]
+                rows = band_halo_extract(a, res, field_res, self.window_size, self.shift_size,
+                                         out=band.buffer("back_send", (B, C, s1, W, D), a.dtype, a.device))
+                pending = band.halo_back_async(rows)
+                x1 = torch.empty(B, L, D, device=x.device, dtype=torch.float32)
+                nargs = (res, field_res, self.window_size, self.shift_size, float(self.norm1.scale_bias), eps)
+                unmerge_adaptive_layernorm_film_add_residual_band(
+                    a, None, x, sc1, sh1, *nargs, out_bf16=x1_bf16, out=x1, rows=(s1, H - s1))
+                unmerge_adaptive_layernorm_film_add_residual_band(
+                    a, pending.wait(), x, sc1, sh1, *nargs, out_bf16=x1_bf16, out=x1, rows=(0, s1))
             if not fuse:
                 # windows (non-pad tokens) + fp32 residual read, fp32 output (+ bf16 copy) written
                 _rec.end("adaln1_unmerge", ev, B * L * D * (e + 4 + 4 + (2 if bf16 else 0)))
@@ -349,8 +370,18 @@ class Swin3DTransformerBlock(nn.Module):
                     x1, h, sc2, sh2, res, self.window_size, next_shift, buf, float(self.norm2.scale_bias), eps)
                 _rec.end("adaln2_partition", ev, B * L * D * (e + 4 + 4 + e))
                 return y
-            y = adaptive_layernorm_film_add_residual_forward(
-                x1, h, sc2, sh2, float(self.norm2.scale_bias), eps, output_fp32=True)
+            if halo_prefetch:
+                # The next shifted block's forward halo first, then the rest of the rows while it
+                # travels.
+                y = torch.empty(B, L, D, device=x.device, dtype=torch.float32)
+                sb2 = float(self.norm2.scale_bias)
+                adaptive_layernorm_film_add_residual_rows(x1, h, sc2, sh2, res, (0, halo_prefetch), sb2, eps, out=y)
+                band.prefetch_forward_halo(y.view(B, C, H, W, D), halo_prefetch, dtype=act)
+                adaptive_layernorm_film_add_residual_rows(x1, h, sc2, sh2, res, (halo_prefetch, H - halo_prefetch),
+                                                          sb2, eps, out=y)
+            else:
+                y = adaptive_layernorm_film_add_residual_forward(
+                    x1, h, sc2, sh2, float(self.norm2.scale_bias), eps, output_fp32=True)
             _rec.end("adaln2", ev, B * L * D * (e + 4 + 4))
             return y
 
@@ -453,8 +484,14 @@ class BasicLayer3D(nn.Module):
         if mods is None:
             mods = [None] * len(self.blocks)
         if band is not None or not x.is_cuda:
-            for blk, m in zip(self.blocks, mods):
-                x = blk(x, c, res, rollout_step, band=band, mods=m)
+            for i, (blk, m) in enumerate(zip(self.blocks, mods)):
+                pre = None
+                if band is not None and band.overlap and i + 1 < len(self.blocks):
+                    # A shifted next block: its forward halo leaves while this block finishes.
+                    nb = self.blocks[i + 1]
+                    _, nss = maybe_adjust_windows(nb.window_size, nb.shift_size, band.field_res)
+                    pre = nss[1] or None
+                x = blk(x, c, res, rollout_step, band=band, mods=m, halo_prefetch=pre)
         else:
             # Each block's norm2 also writes the next block's windows (norm2 + partition fused);
             # one zero-filled buffer per stage keeps the pad slots zero.

@@ -94,6 +94,19 @@ int fa_adaln_film(const void* x, int x_dtype, const void* residual, int residual
                   void* stream);
 
 /*
+ * fa_adaln_film on the token rows (b, c, h, w) of a (B, C*H*W, D) grid with h in
+ * [h_begin, h_begin + h_count) only; every other row of out / out_bf16 is left untouched. Two
+ * calls over complementary ranges write what one fa_adaln_film writes, so a caller can finish
+ * the rows a neighbour waits on first (the next shifted block's halo rows of a latitude band)
+ * and hand them to a transfer while the rest are computed. No reference counterpart.
+ */
+int fa_adaln_film_rows(const void* x, int x_dtype, const void* residual, int residual_dtype,
+                       const void* scale, const void* shift, int mod_dtype, float scale_bias,
+                       float eps, void* out, int out_dtype, void* out_bf16, int64_t B, int64_t C,
+                       int64_t H, int64_t W, int64_t D, int64_t h_begin, int64_t h_count,
+                       void* stream);
+
+/*
  * crop_roll_unmerge fused into the AdaLN above: the AdaLN input row of token (c, h, w) is read
  * straight from the attention windows (B*nW, N, D), so the merged branch tensor is never
  * written. Replaces the pair swin3d.py:751-756 (unmerge) + film.py:101-139 (norm1).
@@ -135,7 +148,9 @@ int fa_adaln_film_partition(const void* x, int x_dtype, const void* residual, in
  *    in C and W; they are the next band's first s original rows (its halo-back buffer).
  *  - fa_crop_roll_unmerge_band / fa_unmerge_adaln_film_band: inverse (plain, or fused with
  *    AdaLN + residual as fa_unmerge_adaln_film); rows 0..s-1 of the band are read from `halo_in`
- *    (B, C, s, W, D, windows dtype), the previous band's halo extract.
+ *    (B, C, s, W, D, windows dtype), the previous band's halo extract. The AdaLN form writes only
+ *    the band rows [h_begin, h_begin + h_count) (0 and H_band for all of them); `halo_in` may be
+ *    NULL when h_begin >= s, so the rows that need no halo can run while it is in flight.
  *
  * Window order inside the band is (c1, h1, w1) over the band's own grid, so the band's windows
  * are the rows [h1_begin, h1_end) of the field's window grid; region ids for a mask are sliced
@@ -159,7 +174,7 @@ int fa_unmerge_adaln_film_band(const void* windows, const void* halo_in, int win
                                void* out, int out_dtype, void* out_bf16, int64_t B, int64_t C,
                                int64_t H_band, int64_t H_field, int64_t W, int64_t D,
                                const int32_t window_size[3], const int32_t shift_size[3],
-                               void* stream);
+                               int64_t h_begin, int64_t h_count, void* stream);
 
 /*
  * Exact GELU, out[i] = x[i] * Phi(x[i]) = x[i] * 0.5 * (1 + erf(x[i] / sqrt(2))) in fp32, rounded to

@@ -109,8 +109,24 @@ def test_band_arguments_return_status_without_a_gpu(lib):
     rc = lib.fa_crop_roll_unmerge_band(p, None, 0, p, 0, 1, 4, 12, 36, 72, 64, ws, ss, None)
     assert rc == _lib.FA_ERR_INVALID and b"halo" in lib.fa_last_error()
     rc = lib.fa_unmerge_adaln_film_band(p, None, 0, p, 0, p, p, 0, 0.0, 1e-5, p, 0, None,
-                                        1, 4, 12, 36, 72, 64, ws, ss, None)
+                                        1, 4, 12, 36, 72, 64, ws, ss, 0, 12, None)
     assert rc == _lib.FA_ERR_INVALID and b"halo" in lib.fa_last_error()
+    # rows that start below the halo depth (s = 3) still need it
+    rc = lib.fa_unmerge_adaln_film_band(p, None, 0, p, 0, p, p, 0, 0.0, 1e-5, p, 0, None,
+                                        1, 4, 12, 36, 72, 64, ws, ss, 2, 10, None)
+    assert rc == _lib.FA_ERR_INVALID and b"halo" in lib.fa_last_error()
+    # row ranges past the band, and an empty range (nothing launched)
+    rc = lib.fa_unmerge_adaln_film_band(p, p, 0, p, 0, p, p, 0, 0.0, 1e-5, p, 0, None,
+                                        1, 4, 12, 36, 72, 64, ws, ss, 6, 7, None)
+    assert rc == _lib.FA_ERR_INVALID and b"row range" in lib.fa_last_error()
+    assert lib.fa_unmerge_adaln_film_band(p, None, 0, p, 0, p, p, 0, 0.0, 1e-5, p, 0, None,
+                                          1, 4, 12, 36, 72, 64, ws, ss, 3, 0, None) == _lib.FA_OK
+    rc = lib.fa_adaln_film_rows(p, 0, p, 0, p, p, 0, 0.0, 1e-5, p, 0, None, 1, 4, 12, 72, 64, -1, 2, None)
+    assert rc == _lib.FA_ERR_INVALID and b"row range" in lib.fa_last_error()
+    rc = lib.fa_adaln_film_rows(p, 0, p, 0, p, p, 0, 0.0, 1e-5, p, 0, None, 1, 4, 12, 72, 64, 10, 3, None)
+    assert rc == _lib.FA_ERR_INVALID and b"row range" in lib.fa_last_error()
+    assert lib.fa_adaln_film_rows(p, 0, p, 0, p, p, 0, 0.0, 1e-5, p, 0, None, 1, 4, 12, 72, 64, 5, 0,
+                                  None) == _lib.FA_OK
     # band taller than the field
     rc = lib.fa_band_halo_extract(p, 0, p, 0, 1, 4, 42, 36, 72, 64, ws, ss, None)
     assert rc == _lib.FA_ERR_INVALID

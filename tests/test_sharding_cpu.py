@@ -191,6 +191,35 @@ def test_gloo_silent_peer_times_out():
     assert elapsed < 15 and "rank 0" in msg
 
 
+@pytest.mark.parametrize("world", [2, 3])
+def test_prefetched_forward_halo(world):
+    """A forward halo issued early by the producing block (``prefetch_forward_halo``) is the one
+    the shifted block's ``halo_forward`` returns: the next band's first rows. A prefetch issued for
+    another tensor is refused, not silently used."""
+    field_res = (4, 36, 72)
+    x = _field(2, field_res)
+
+    def fn(rank, ring):
+        ctx = sharding.BandContext(field_res, WS, rank, world, ring=ring, timeout_s=30)
+        xb = torch.from_numpy(np.ascontiguousarray(x[:, :, ctx.h_begin:ctx.h_end]))
+        direct = ctx.halo_forward(xb, 3).clone()
+        handle = ctx.prefetch_forward_halo(xb, 3)
+        got = ctx.halo_forward(xb, 3).clone()
+        nb = ctx.bounds[ctx.next][0]
+        ok = torch.equal(direct, got) and np.array_equal(got.numpy(), x[:, :, nb:nb + 3])
+        ok = ok and handle.recv.data_ptr() == ctx.buffer("fwd_recv", tuple(got.shape), got.dtype, "cpu").data_ptr()
+        ctx.prefetch_forward_halo(xb, 3)
+        try:
+            ctx.halo_forward(xb.clone(), 3)
+            refused = False
+        except RuntimeError:
+            refused = True
+        return ok, refused
+
+    for ok, refused in sharding.run_ranks(world, fn):
+        assert ok and refused
+
+
 def test_nccl_exchange_deadline_bookkeeping(monkeypatch):
     """The stream-ordered (NCCL) exchanges leave events that later exchanges and ``wait`` check:
     finished ones are dropped, and the oldest unfinished one past ``timeout_s`` raises

@@ -109,8 +109,44 @@ def test_band_unmerge_adaln_bit_exact(shift, wdt):
                 wbs[r], halo_in, res_b, scale, shf, band_res, field_res, WS, shift, out_bf16=ob)
             assert torch.equal(y.view(1, C, b - a, W, D), full5[:, :, a:b]), (world, r)
             assert torch.equal(ob.view(1, C, b - a, W, D), full_bf5[:, :, a:b])
+            # The same rows in two launches: the rows past the halo depth first, without the
+            # halo (as while it is in flight), then the first s rows.
+            y2 = torch.full_like(y, float("nan"))
+            ob2 = torch.full_like(ob, float("nan"))
+            fa.unmerge_adaptive_layernorm_film_add_residual_band(
+                wbs[r], None, res_b, scale, shf, band_res, field_res, WS, shift, out_bf16=ob2, out=y2,
+                rows=(s, b - a - s))
+            fa.unmerge_adaptive_layernorm_film_add_residual_band(
+                wbs[r], halo_in, res_b, scale, shf, band_res, field_res, WS, shift, out_bf16=ob2, out=y2,
+                rows=(0, s))
+            assert torch.equal(y2, y) and torch.equal(ob2, ob), (world, r)
         if s == 0:
             break
+
+
+@pytest.mark.parametrize("xdt", [torch.float32, torch.bfloat16])
+def test_adaln_rows_split_equals_full(xdt):
+    """Two row-range launches (the first s rows of every C slab, then the rest) write exactly what
+    one full AdaLN + residual launch writes."""
+    res, D = (4, 36, 72), 256
+    C, H, W = res
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(2, C * H * W, D, generator=g).to(xdt).cuda()
+    resid = torch.randn(2, C * H * W, D, generator=g).cuda()
+    scale = (torch.randn(2, 1, D, generator=g) * 0.1).cuda()
+    shf = (torch.randn(2, 1, D, generator=g) * 0.1).cuda()
+    full_bf = torch.empty(2, C * H * W, D, dtype=torch.bfloat16, device="cuda")
+    full = fa.adaptive_layernorm_film_add_residual_forward(resid, x, scale, shf, 0.0, 1e-5, output_fp32=True,
+                                                           out_bf16=full_bf)
+    out = torch.full_like(full, float("nan"))
+    out_bf = torch.full_like(full_bf, float("nan"))
+    fa.adaptive_layernorm_film_add_residual_rows(resid, x, scale, shf, res, (0, 3), 0.0, 1e-5, out=out,
+                                                 out_bf16=out_bf)
+    part = out.view(2, C, H, W, D)
+    assert torch.isnan(part[:, :, 3:]).all() and not torch.isnan(part[:, :, :3]).any()
+    fa.adaptive_layernorm_film_add_residual_rows(resid, x, scale, shf, res, (3, H - 3), 0.0, 1e-5, out=out,
+                                                 out_bf16=out_bf)
+    assert torch.equal(out, full) and torch.equal(out_bf, full_bf)
 
 
 def test_band_rejects_bad_geometry():
