@@ -93,7 +93,7 @@ __device__ __forceinline__ void store_tile_half(uint32_t ta, int col0, int row0,
         const int si = idx & 31;
         const float2 bf = unpack_bf16x2(bb[e]);
         float2 y = make_float2(__uint_as_float(src[si]) + bf.x, __uint_as_float(src[si + 1]) + bf.y);
-        if constexpr (kGelu) y = gelu2_poly(y);
+        if constexpr (kGelu) y = gelu2_bf16out(y);
         pk[4 * v + e] = pack_bf16x2(y.x, y.y);
       }
     }
