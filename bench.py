@@ -505,10 +505,12 @@ def measure_sharded(dist, rank, world, local, steps, warmup) -> dict:
         for p in layer.parameters():
             p.normal_(0.0, 0.02)
     layer = layer.to(dev).eval()
-    # The halo exchanges get their own group with high-priority NCCL streams (they overlap the
-    # normalisation of the rows that do not need them).
-    group = halo_process_group(timeout_s=120) if dist is not None else None
-    ctx = BandContext(cfg["field"], cfg["window"], rank, world, group=group, timeout_s=120)
+    ctx = BandContext(cfg["field"], cfg["window"], rank, world, group=None, timeout_s=120)
+    if dist is not None:
+        # The world group, or with the overlapped exchanges (FA_BAND_OVERLAP=1) their own group
+        # with high-priority NCCL streams.
+        group = halo_process_group(timeout_s=120) if ctx.overlap else dist.group.WORLD
+        ctx = BandContext(cfg["field"], cfg["window"], rank, world, group=group, timeout_s=120)
     # Every rank draws the same whole field and keeps its band, so the banded result can be
     # checked against the whole field run unsharded on one GPU.
     gen = torch.Generator(device=dev).manual_seed(99)

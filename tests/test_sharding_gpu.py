@@ -173,7 +173,8 @@ def _stage(dim, heads, depth, precision, seed=5):
 
 @pytest.mark.parametrize("precision,tol", [("fp32", 1e-6), ("bf16_mixed", 5e-3)])
 @pytest.mark.parametrize("world", [2, 3])
-def test_sharded_stage_threads_match_field(precision, tol, world):
+@pytest.mark.parametrize("overlap", [False, True])
+def test_sharded_stage_threads_match_field(precision, tol, world, overlap):
     field_res, dim, heads = (4, 36, 72), 128, 2
     C, H, W = field_res
     layer = _stage(dim, heads, 2, precision)
@@ -186,7 +187,7 @@ def test_sharded_stage_threads_match_field(precision, tol, world):
     x5 = x.view(1, C, H, W, dim)
 
     def fn(rank, ring):
-        ctx = sharding.BandContext(field_res, WS, rank, world, ring=ring, timeout_s=60)
+        ctx = sharding.BandContext(field_res, WS, rank, world, ring=ring, timeout_s=60, overlap=overlap)
         a, b = ctx.h_begin, ctx.h_end
         xb = x5[:, :, a:b].reshape(1, -1, dim).contiguous()
         with torch.no_grad():
@@ -208,7 +209,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, q, precision="fp32"):
+def _nccl_worker(rank, world, port, q, precision="fp32", overlap=False):
     import datetime
 
     import torch.distributed as dist
@@ -226,7 +227,8 @@ def _nccl_worker(rank, world, port, q, precision="fp32"):
         g = torch.Generator().manual_seed(9)
         x = torch.randn(1, C * H * W, dim, generator=g).cuda()
         c = torch.randn(1, dim, generator=g).cuda()
-        ctx = sh.BandContext(field_res, WS, rank, world, timeout_s=60)
+        group = sh.halo_process_group(timeout_s=60) if overlap else None
+        ctx = sh.BandContext(field_res, WS, rank, world, group=group, timeout_s=60, overlap=overlap)
         a, b = ctx.h_begin, ctx.h_end
         with torch.no_grad():
             want, _ = layer(x, c, field_res)
@@ -241,16 +243,18 @@ def _nccl_worker(rank, world, port, q, precision="fp32"):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("precision,tol", [("fp32", 1e-6), ("bf16_mixed", 5e-3)])
-def test_sharded_stage_nccl_two_gpus(precision, tol):
+@pytest.mark.parametrize("overlap", [False, True])
+def test_sharded_stage_nccl_two_gpus(precision, tol, overlap):
     """Two ranks over NCCL (NVLS off): each band of the sharded stage against the same rows of the
-    unsharded stage. In bf16_mixed the forward halo travels in bf16; cuBLAS may pick another
-    algorithm for the band's row count, hence the bf16 tolerance."""
+    unsharded stage, with the exchanges in line or on the side stream (high-priority halo group).
+    In bf16_mixed the forward halo travels in bf16; cuBLAS may pick another algorithm for the
+    band's row count, hence the bf16 tolerance."""
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q, precision)) for r in range(2)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q, precision, overlap)) for r in range(2)]
     for p in procs:
         p.start()
     out = {}
