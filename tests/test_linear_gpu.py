@@ -72,6 +72,40 @@ def test_pair_and_single_kernels_agree_at_config4_shapes(M, N, K, monkeypatch):
     assert torch.equal(outs[0], outs[1])
 
 
+@pytest.mark.parametrize("kernel", ["single", "pair"])
+def test_gelu_epilogue_over_the_bf16_range(kernel, monkeypatch):
+    """The epilogue's GELU on every finite bf16 value of magnitude up to 64: a 0/1 weight matrix
+    routes each input value unchanged to one output element, so the epilogue sees exactly that
+    value. Each result is the exact GELU rounded to bf16 or one bf16 unit away from it (rarely);
+    below x = -7 (|GELU| < 1e-10) the fitted q overestimates the exact one, so there the bound is an
+    absolute 1e-6, as for the standalone kernel's tail; results below the fp32 normal range
+    (denormal inputs, or x * Phi(x) under 2^-126) may flush to zero."""
+    monkeypatch.setenv("FA_GEMM_KERNEL", kernel)
+    bits = torch.arange(0, 65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    vals = bits[torch.isfinite(bits.float()) & (bits.float().abs() <= 64)]
+    K, N = 64, 256
+    M = -(-vals.numel() // K)
+    x = torch.zeros(M * K, dtype=torch.bfloat16)
+    x[: vals.numel()] = vals
+    x = x.view(M, K).cuda()
+    w = torch.zeros(N, K, dtype=torch.bfloat16)
+    w[torch.arange(N), torch.arange(N) % K] = 1
+    b = torch.zeros(N, dtype=torch.bfloat16)
+    got = linear_bias_act(x, w.cuda(), b.cuda(), act="gelu").cpu()
+    inp = x.cpu().double()[:, torch.arange(N) % K]
+    exact = 0.5 * inp * (1.0 + torch.erf(inp / math.sqrt(2.0)))
+    want = exact.float().bfloat16()
+    same = got == want
+    # one bf16 unit: the spacing at the rounded exact value
+    ulp = (want.float().abs() * 2.0 ** -7).clamp_min(2.0 ** -133)
+    near = (got.float() - want.float()).abs() <= ulp * 1.01
+    tail = (inp < -7) & ((got.double() - exact).abs() <= 1e-6)
+    tiny = (exact.abs() < 2.0 ** -125) & (got.float().abs() <= 2.0 ** -125)
+    assert (near | tail | tiny).all()
+    body = (inp >= -7) & (exact.abs() >= 2.0 ** -125)
+    assert (~same[body]).float().mean().item() < 2e-3
+
+
 def test_linear_bias_act_batched_input_and_strided_rows():
     g = torch.Generator().manual_seed(1)
     x = torch.randn(3, 50, 640, generator=g).bfloat16().cuda()[..., :512]  # row stride 640
