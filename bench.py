@@ -236,7 +236,7 @@ OPERATORS = {
     "attention": ("hbm", "this library: attn_tc_bf16_kernel (tcgen05)"),
     "proj_gemm": ("tensor", "this library: tcgen05 GEMM, bias epilogue (CTA pair, 256 x 256 tiles)"),
     "adaln1_unmerge": ("hbm", "this library: adaln_kernel (unmerge-fused, bf16 copy)"),
-    "fc1_gelu_gemm": ("tensor", "this library: tcgen05 GEMM + GELU epilogue (single CTA at K=512, CTA pair above)"),
+    "fc1_gelu_gemm": ("tensor", "this library: tcgen05 GEMM + GELU epilogue (CTA pair, 256 x 256 tiles)"),
     "fc2_gemm": ("tensor", "cuBLAS bf16 GEMM at stage 2, this library's CTA-pair GEMM at stage 3"),
     "adaln2_partition": ("hbm", "this library: adaln_kernel (next-partition fused)"),
     "adaln2": ("hbm", "this library: adaln_kernel"),

@@ -485,12 +485,12 @@ extern "C" int fa_linear_bias_act(const void* a, const void* w, const void* bias
              "a, w, bias and out must be 16-byte aligned");
   FA_REQUIRE(lda >= K && ldw >= K && ldo >= N && lda % 8 == 0 && ldw % 8 == 0 && ldo % 8 == 0, FA_ERR_INVALID,
              "row strides must cover the rows and be multiples of 8 elements");
-  // Kernel: the CTA-pair kernel (256 x 256 tiles, two thirds of the shared-memory fill per FLOP)
-  // except for the GELU epilogue at K < 1024, where the epilogue sets the tile period and the
-  // pair's coupled tiles measured slower (config-4 stage 1 fc1: 0.59 against 0.55 ms);
-  // FA_GEMM_KERNEL=single|pair forces one (tests).
+  // Kernel: the CTA-pair kernel (256 x 256 tiles, two thirds of the shared-memory fill per FLOP);
+  // it measured at least as fast as the single-CTA kernel at every config-4 linear once its
+  // accumulator release stopped paying a cluster-scope memory barrier (stage-1 fc1 + GELU 0.47-0.49
+  // against 0.48-0.49 ms). FA_GEMM_KERNEL=single|pair forces one (tests).
   const int choice = gemm::kernel_choice();
-  const bool use_pair = choice == 2 || (choice == 0 && !(act == FA_ACT_GELU && K < 1024));
+  const bool use_pair = choice != 1;
   const int64_t tile_m = use_pair ? 256 : gemm::kBM;
   CUtensorMap ma, mw, mo;
   int rc;

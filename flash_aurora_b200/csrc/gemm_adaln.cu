@@ -298,7 +298,7 @@ gemm_adaln_pair_kernel(const __grid_constant__ CUtensorMap tma, const __grid_con
       __syncwarp();
       if (lane == 0) {
         if (rank == 0) mbar_arrive(BAR(kAccEmpty));
-        else mbar_arrive_remote(map_shared_rank(BAR(kAccEmpty), 0));
+        else mbar_arrive_remote_cluster_release(map_shared_rank(BAR(kAccEmpty), 0));
       }
       epi_bar();  // every row of the h tile and every half-row sum is written
       // E1b (thread = row, the four half-0 warps): mean from the two half-row sums, then the sum
