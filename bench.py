@@ -407,10 +407,14 @@ def run_b200(args) -> None:
         # End to end from pinned host memory through the public API: every step uploads its
         # input and downloads its full output; HostPipeline overlaps those copies with the
         # neighbouring steps' compute (two host input and two host output buffers in rotation).
+        # Two captures of the step (each with its own memory pool); each step uploads into its
+        # slot's static input and downloads that slot's static output directly.
+        from flash_aurora_b200.graph import CapturedStep as _CS
         from flash_aurora_b200.pipeline import HostPipeline
+        slots = [graphed, _CS(step, x, warmup=0)]
         x_host = [x.cpu().pin_memory(), (x + 1.0).cpu().pin_memory()]
         out_host = [torch.empty(tuple(y.shape), dtype=y.dtype, pin_memory=True) for _ in range(2)]
-        pipe = HostPipeline(graphed, dev)
+        pipe = HostPipeline(slots, dev)
         pipe.run(x_host[:1], out_host[:1])  # warm the pipeline's streams and buffers
         pipe.wait()
         _barrier(dist)

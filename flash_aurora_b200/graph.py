@@ -17,7 +17,7 @@ from typing import Callable
 
 import torch
 
-__all__ = ["CapturedStep"]
+__all__ = ["CapturedStep", "capture_slots"]
 
 
 class CapturedStep:
@@ -84,3 +84,15 @@ class CapturedStep:
         self.static_input.copy_(x)
         self.graph.replay()
         return self.static_output.clone()
+
+
+def capture_slots(fn: Callable[[torch.Tensor], torch.Tensor], example: torch.Tensor, n: int = 2,
+                  warmup: int = 2) -> list[CapturedStep]:
+    """``n`` captures of the same step, each with its own static input and output and its own
+    memory pool, for :class:`~flash_aurora_b200.pipeline.HostPipeline`: while slot ``k``
+    computes, the previous slot's output is still being downloaded and the next slot's input is
+    being uploaded, with no device-side copy in or out of the graphs. (Two captures sharing one
+    pool produced wrong outputs in this rotation, so each slot keeps its own intermediates.)"""
+    if n < 1:
+        raise ValueError("n must be >= 1")
+    return [CapturedStep(fn, example, warmup=warmup if i == 0 else 0) for i in range(n)]

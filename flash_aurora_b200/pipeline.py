@@ -8,6 +8,12 @@ copies use the copy engines, not the SMs, so they can run under the neighbouring
 stream while step ``i`` computes, and step ``i``'s download runs on another copy stream while
 step ``i + 1`` computes. Every step still moves its own input and output across PCIe; only the
 waiting is removed. Ordering is by CUDA events only; the host never blocks inside ``run``.
+
+The step is either a callable (the pipeline keeps ``depth`` device input buffers) or a sequence of
+captured graphs (:func:`~flash_aurora_b200.graph.capture_slots`): then step ``i`` uploads straight
+into slot ``i % len(slots)``'s static input, replays it and downloads its static output, so no
+device-side copy enters or leaves the graphs; a slot is replayed again only after the download of
+its previous output.
 :meth:`HostPipeline.wait` is the sync point: it blocks until the last download has landed and
 then checks the kernels' device status words (a pipeline wait that gave up inside a kernel is
 reported there, not by the launch), raising :class:`~flash_aurora_b200.status.DeviceStatusError`.
@@ -30,7 +36,14 @@ class HostPipeline:
     host tensors (pageable memory works but serialises the copies).
     """
 
-    def __init__(self, step: Callable[[torch.Tensor], torch.Tensor], device, depth: int = 2) -> None:
+    def __init__(self, step, device, depth: int = 2) -> None:
+        self.slots = None
+        if isinstance(step, (list, tuple)):
+            # Captured slots: objects with static_input, static_output and replay().
+            if not step or not all(hasattr(t, "replay") and hasattr(t, "static_input") for t in step):
+                raise ValueError("slots must be a non-empty sequence of captured steps")
+            self.slots = list(step)
+            depth = len(self.slots)
         if depth < 1:
             raise ValueError("depth must be >= 1")
         self.step = step
@@ -52,6 +65,8 @@ class HostPipeline:
         n = len(host_inputs)
         if n == 0:
             return
+        if self.slots is not None:
+            return self._run_slots(host_inputs, host_outputs)
         compute = torch.cuda.current_stream(self.device)
         bufs = self._buffers(host_inputs[0])
         uploaded = [torch.cuda.Event() for _ in range(n)]
@@ -90,6 +105,46 @@ class HostPipeline:
         # run() returns bracket all the copies.
         compute.wait_event(last_down)
         self._last = last_down
+
+    def _run_slots(self, host_inputs, host_outputs) -> None:
+        n, k = len(host_inputs), len(self.slots)
+        compute = torch.cuda.current_stream(self.device)
+        for t in self.slots:
+            if tuple(t.static_input.shape) != tuple(host_inputs[0].shape):
+                raise ValueError(f"slots captured for {tuple(t.static_input.shape)}, inputs are "
+                                 f"{tuple(host_inputs[0].shape)}")
+        uploaded = [torch.cuda.Event() for _ in range(n)]
+        computed = [torch.cuda.Event() for _ in range(n)]    # replay i done: slot input and output free to reuse
+        downloaded = [torch.cuda.Event() for _ in range(n)]  # output i in host memory
+        start = torch.cuda.Event()
+        start.record(compute)
+        self.up.wait_event(start)
+        self.down.wait_event(start)
+
+        def upload(i: int) -> None:
+            with torch.cuda.stream(self.up):
+                if i >= k:
+                    self.up.wait_event(computed[i - k])  # the slot's previous replay read its input
+                self.slots[i % k].static_input.copy_(host_inputs[i], non_blocking=True)
+                uploaded[i].record(self.up)
+
+        for i in range(min(k - 1, n)):
+            upload(i)
+        for i in range(n):
+            if i + k - 1 < n:
+                upload(i + k - 1)
+            slot = self.slots[i % k]
+            compute.wait_event(uploaded[i])
+            if i >= k:
+                compute.wait_event(downloaded[i - k])  # the slot's previous output has left
+            slot.replay()
+            computed[i].record(compute)
+            with torch.cuda.stream(self.down):
+                self.down.wait_event(computed[i])
+                host_outputs[i].copy_(slot.static_output, non_blocking=True)
+                downloaded[i].record(self.down)
+        compute.wait_event(downloaded[n - 1])
+        self._last = downloaded[n - 1]
 
     def wait(self, check_status: bool = True) -> None:
         """Block until the outputs of the last :meth:`run` are in host memory; then, with
