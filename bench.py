@@ -344,6 +344,27 @@ def same_box_bars(dev) -> dict:
                     "CuTe/Triton kernels need their JIT sources at run time and are not on this box"}
 
 
+def _bind_host_to_gpu(local: int) -> str:
+    """Pin this rank's host threads to the CPUs NVML reports as closest to its GPU, so that the
+    pinned host buffers of the end-to-end leg (allocated, and first touched, afterwards) sit on
+    the GPU's own NUMA node. Only a process CPU mask changes; nothing on the GPU. Returns what was
+    done, for the JSON line."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(local).uuid)
+        h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}")
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+        cpus = {w * 64 + b for w, word in enumerate(words) for b in range(64) if (word >> b) & 1}
+        cpus &= set(os.sched_getaffinity(0))
+        if not cpus:
+            return "not bound (NVML gave no CPUs)"
+        os.sched_setaffinity(0, cpus)
+        return f"bound to {len(cpus)} GPU-local CPUs"
+    except Exception as exc:  # noqa: BLE001 - optional
+        return f"not bound ({type(exc).__name__})"
+
+
 def run_b200(args) -> None:
     from flash_aurora_b200 import recorder as R
     from flash_aurora_b200.status import check_device_status
@@ -352,6 +373,9 @@ def run_b200(args) -> None:
     dist, rank, world, local = _dist()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    # Several ranks share the host: keep each one's copies on its GPU's NUMA node. A single rank
+    # keeps every core (its CPU baseline uses them all).
+    host_binding = _bind_host_to_gpu(local) if world > 1 else "not bound (one rank)"
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     model = Swin3DTransformerBackbone(**CONFIG4, precision="bf16_mixed").to(dev).eval()
     init_random_weights_(model, generator=gen)
@@ -459,7 +483,7 @@ def run_b200(args) -> None:
                    "execution": "step captured once as a CUDA graph and replayed (static shapes)",
                    "blocks": n_blocks},
         "e2e": {"value": round(e2e_ms, 2), "unit": UNIT, "h2d_bytes_per_step": x.numel() * x.element_size(),
-                "d2h_bytes_per_step": y.numel() * y.element_size()},
+                "d2h_bytes_per_step": y.numel() * y.element_size(), "host_threads": host_binding},
         "gpu_launches": (launches["this_library"] * args.steps) if "this_library" in launches else None,
         "launches_per_step": launches,
         "roofline": roofline,
