@@ -535,7 +535,7 @@ def measure_sharded(dist, rank, world, local, steps, warmup) -> dict:
     layer = layer.to(dev).eval()
     ctx = BandContext(cfg["field"], cfg["window"], rank, world, group=None, timeout_s=120)
     if dist is not None:
-        # The world group, or with the overlapped exchanges (FA_BAND_OVERLAP=1) their own group
+        # The world group, or with the overlapped exchanges (default from four ranks) their own group
         # with high-priority NCCL streams.
         group = halo_process_group(timeout_s=120) if ctx.overlap else dist.group.WORLD
         ctx = BandContext(cfg["field"], cfg["window"], rank, world, group=group, timeout_s=120)

@@ -136,12 +136,14 @@ class BandContext:
         self.group = group
         self.ring = ring
         self.timeout_s = float(timeout_s)
-        # Overlap the halo exchanges with the rows that do not need them (overlap=True, or the
-        # FA_BAND_OVERLAP=1 environment setting). Off by default: on two B200s the config-5 stage
-        # measured 0.4-0.7 ms per 52 ms step slower with it (the two extra short launches per
-        # exchange cost more than the exchange they hide).
+        # Overlap the halo exchanges with the rows that do not need them. Default: from four
+        # ranks on (FA_BAND_OVERLAP=0 / 1 or overlap=False / True override it). Measured on the
+        # config-5 stage: on two B200s 0.4-0.7 ms per 52 ms step slower with it (the two extra
+        # short launches per exchange cost more than the exchange they hide), on four 0.35-0.4 ms
+        # per 25 ms step faster (smaller bands, the same exchanges).
         if overlap is None:
-            overlap = os.environ.get("FA_BAND_OVERLAP", "0") == "1"
+            env = os.environ.get("FA_BAND_OVERLAP")
+            overlap = (env == "1") if env in ("0", "1") else self.world >= 4
         self.overlap = bool(overlap)
         self.prev = (self.rank - 1) % self.world
         self.next = (self.rank + 1) % self.world
