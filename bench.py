@@ -245,6 +245,8 @@ OPERATORS = {
 }
 # DRAM bytes / algorithmic bytes from ncu captures of the kernel (profiles/): the attention at
 # config 2 and the fused fc1 + GELU at the config-4 stage-1 shape.
+# fc1 + GELU at stage 1 on the CTA-pair kernel: 267.7 MB read + 1003 MB written against 1329 MB
+# algorithmic (profiles/gemm_fc1_gelu_single_vs_pair_config4_s1.md; the single-CTA kernel, 0.956 too).
 TRAFFIC_RATIOS = {"attention": TRAFFIC_RATIO, "fc1_gelu_gemm": 0.956}
 
 
