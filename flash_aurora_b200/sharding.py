@@ -337,6 +337,9 @@ class BandContext:
         dtype = x_band.dtype if dtype is None else dtype
         send = self.buffer("fwd_send", (B, C, s, W, D), dtype, x_band.device)
         recv = self.buffer("fwd_recv", (B, C, s, W, D), dtype, x_band.device)
+        if self._overlapped(recv):
+            # The side stream reads x_band: keep its memory from the allocator until it has.
+            x_band.record_stream(self.comm_stream(x_band.device))
         handle = self.exchange_async(send, recv, dst=self.prev, src=self.next,
                                      stage=lambda: send.copy_(x_band[:, :, :s]))
         if _keep:
