@@ -434,10 +434,12 @@ def run_b200(args) -> None:
         # input and downloads its full output; HostPipeline overlaps those copies with the
         # neighbouring steps' compute (two host input and two host output buffers in rotation).
         # Two captures of the step (each with its own memory pool); each step uploads into its
-        # slot's static input and downloads that slot's static output directly.
-        from flash_aurora_b200.graph import CapturedStep as _CS
+        # slot's static input and downloads that slot's output directly: the skip half of the
+        # final concatenation as soon as the first encoder layer has written it, the decoder half
+        # after the replay.
+        from flash_aurora_b200.graph import capture_backbone_slots
         from flash_aurora_b200.pipeline import HostPipeline
-        slots = [graphed, _CS(step, x, warmup=0)]
+        slots = capture_backbone_slots(model, lead, 0, PATCH_RES, x, n=2, warmup=1)
         x_host = [x.cpu().pin_memory(), (x + 1.0).cpu().pin_memory()]
         out_host = [torch.empty(tuple(y.shape), dtype=y.dtype, pin_memory=True) for _ in range(2)]
         pipe = HostPipeline(slots, dev)

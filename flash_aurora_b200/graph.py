@@ -17,7 +17,7 @@ from typing import Callable
 
 import torch
 
-__all__ = ["CapturedStep", "capture_slots"]
+__all__ = ["CapturedStep", "capture_slots", "capture_backbone_slots"]
 
 
 class CapturedStep:
@@ -96,3 +96,37 @@ def capture_slots(fn: Callable[[torch.Tensor], torch.Tensor], example: torch.Ten
     if n < 1:
         raise ValueError("n must be >= 1")
     return [CapturedStep(fn, example, warmup=warmup if i == 0 else 0) for i in range(n)]
+
+
+def capture_backbone_slots(model, lead_time, rollout_step: int, patch_res, example: torch.Tensor,
+                           n: int = 2, warmup: int = 2) -> list[CapturedStep]:
+    """:func:`capture_slots` for a :class:`~flash_aurora_b200.swin3d.Swin3DTransformerBackbone`
+    forward whose output is ``cat([decoder output, skip], -1)``: each slot also carries ``skip``
+    (its graph's first-encoder-layer output, the right half of that concatenation) and
+    ``skip_ready``, an event recorded inside the graph right after ``skip`` is written, so that
+    :class:`~flash_aurora_b200.pipeline.HostPipeline` downloads that half while the decoder still
+    runs and only the left half after the replay."""
+    if n < 1:
+        raise ValueError("n must be >= 1")
+    step = lambda x: model(x, lead_time=lead_time, rollout_step=rollout_step, patch_res=patch_res)
+    slots = []
+    try:
+        for i in range(n):
+            ev = torch.cuda.Event(external=True)
+            seen: list = []
+
+            def hook(t: torch.Tensor, ev=ev, seen=seen) -> None:
+                ev.record()
+                seen.append(t)
+
+            model.skip_hook = hook
+            slot = CapturedStep(step, example, warmup=warmup if i == 0 else 0)
+            slot.skip = seen[-1]  # the tensor the capture recorded (the graph rewrites it in place)
+            slot.skip_ready = ev
+            if (slot.static_output.dim() != 3 or slot.skip.shape[:2] != slot.static_output.shape[:2]
+                    or 2 * slot.skip.shape[-1] != slot.static_output.shape[-1]):
+                raise ValueError("the step's output is not cat([decoder output, skip], -1)")
+            slots.append(slot)
+    finally:
+        model.skip_hook = None
+    return slots

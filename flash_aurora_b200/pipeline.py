@@ -28,6 +28,28 @@ import torch
 __all__ = ["HostPipeline"]
 
 
+def _download_half(host_out: torch.Tensor, src: torch.Tensor, right: bool, stream) -> None:
+    """One strided device-to-host copy into the left or right half of the last dimension of the
+    contiguous pinned ``host_out`` (rows of ``2 * D`` elements): from ``src`` rows of ``D`` elements
+    (``right``), or from the left half of ``src`` rows of ``2 * D`` elements."""
+    from cuda.bindings import runtime as rt
+
+    if not host_out.is_contiguous() or host_out.device.type != "cpu":
+        raise ValueError("host outputs must be contiguous host tensors")
+    if src.stride(-1) != 1 or not (src.is_contiguous() or src.numel() == src.shape[-2] * src.shape[-1]):
+        raise ValueError("the source must be a contiguous tensor of rows")
+    e = host_out.element_size()
+    d2 = host_out.shape[-1]
+    rows = host_out.numel() // d2
+    width = (d2 // 2) * e
+    dst = host_out.data_ptr() + (width if right else 0)
+    spitch = src.stride(-2) * e if src.dim() >= 2 else width
+    err, = rt.cudaMemcpy2DAsync(dst, d2 * e, src.data_ptr(), spitch, width, rows,
+                                rt.cudaMemcpyKind.cudaMemcpyDeviceToHost, stream.cuda_stream)
+    if err != rt.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"cudaMemcpy2DAsync failed: {err}")
+
+
 class HostPipeline:
     """``run(host_inputs, host_outputs)`` computes ``host_outputs[i] = step(host_inputs[i])``.
 
@@ -140,8 +162,16 @@ class HostPipeline:
             slot.replay()
             computed[i].record(compute)
             with torch.cuda.stream(self.down):
-                self.down.wait_event(computed[i])
-                host_outputs[i].copy_(slot.static_output, non_blocking=True)
+                if getattr(slot, "skip_ready", None) is not None:
+                    # The skip half leaves as soon as the graph has written it, the decoder half
+                    # after the replay (capture_backbone_slots).
+                    self.down.wait_event(slot.skip_ready)
+                    _download_half(host_outputs[i], slot.skip, right=True, stream=self.down)
+                    self.down.wait_event(computed[i])
+                    _download_half(host_outputs[i], slot.static_output, right=False, stream=self.down)
+                else:
+                    self.down.wait_event(computed[i])
+                    host_outputs[i].copy_(slot.static_output, non_blocking=True)
                 downloaded[i].record(self.down)
         compute.wait_event(downloaded[n - 1])
         self._last = downloaded[n - 1]

@@ -32,7 +32,7 @@ from __future__ import annotations
 import contextlib
 import math
 from datetime import timedelta
-from typing import Optional
+from typing import Callable, Optional
 
 import numpy as np
 import torch
@@ -557,6 +557,9 @@ class Swin3DTransformerBackbone(nn.Module):
         super().__init__()
         self.precision = _check_precision(precision)
         self.workspace_pool = workspace_pool
+        # Called with the first encoder layer's output, the skip half of the final concatenation,
+        # as soon as it exists (a serving pipeline starts its download there); None: nothing.
+        self.skip_hook: Optional[Callable[[torch.Tensor], None]] = None
         self.window_size = tuple(window_size) if isinstance(window_size, (tuple, list)) else (window_size,) * 3
         self.num_encoder_layers = len(encoder_depths)
         self.num_decoder_layers = len(decoder_depths)
@@ -652,6 +655,8 @@ class Swin3DTransformerBackbone(nn.Module):
             for i, layer in enumerate(self.encoder_layers):
                 x, x_unscaled = layer(x, c, all_res[i], rollout_step=rollout_step, mods=mods[layer])
                 skips.append(x_unscaled)
+                if i == 0 and self.skip_hook is not None:
+                    self.skip_hook(x_unscaled)
             for i, layer in enumerate(self.decoder_layers):
                 index = self.num_decoder_layers - i - 1
                 x, _ = layer(x, c, all_res[index], padded[index - 1], rollout_step=rollout_step,

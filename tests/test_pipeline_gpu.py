@@ -94,3 +94,33 @@ def test_captured_slots_pipeline_matches_eager(n_slots):
         pipe.run(xs[::-1], [rot[i % 2] for i in range(5)])  # two host buffers in rotation
         pipe.wait()
     assert torch.equal(rot[0], wants[0]) and torch.equal(rot[1], wants[1])
+
+
+def test_backbone_slots_download_the_skip_half_early():
+    """Backbone slots: the skip half of every output leaves after the first encoder layer (an event
+    recorded inside the graph), the decoder half after the replay; every host output equals the
+    eager forward of its own input, bit for bit, over more steps than slots."""
+    from datetime import timedelta
+
+    from flash_aurora_b200.graph import capture_backbone_slots
+    from flash_aurora_b200.swin3d import Swin3DTransformerBackbone, init_random_weights_
+
+    dev = torch.device("cuda", 0)
+    model = Swin3DTransformerBackbone(embed_dim=128, encoder_depths=(2, 2), encoder_num_heads=(2, 4),
+                                      decoder_depths=(2, 2), decoder_num_heads=(4, 2), window_size=(2, 6, 12),
+                                      precision="bf16_mixed").to(dev).eval()
+    init_random_weights_(model, generator=torch.Generator(device=dev).manual_seed(7))
+    res = (4, 24, 48)
+    lead = timedelta(hours=6)
+    g = torch.Generator().manual_seed(8)
+    xs = [torch.randn(1, res[0] * res[1] * res[2], 128, generator=g).pin_memory() for _ in range(5)]
+    with torch.no_grad():
+        wants = [model(x.to(dev), lead_time=lead, rollout_step=0, patch_res=res).cpu() for x in xs]
+        slots = capture_backbone_slots(model, lead, 0, res, xs[0].to(dev), n=2)
+        assert model.skip_hook is None
+        outs = [torch.full(tuple(wants[0].shape), float("nan")).pin_memory() for _ in range(5)]
+        pipe = HostPipeline(slots, dev)
+        pipe.run(xs, outs)
+        pipe.wait()
+    for a, b in zip(outs, wants):
+        assert torch.equal(a, b)
