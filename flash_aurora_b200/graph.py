@@ -121,6 +121,8 @@ def capture_backbone_slots(model, lead_time, rollout_step: int, patch_res, examp
 
             model.skip_hook = hook
             slot = CapturedStep(step, example, warmup=warmup if i == 0 else 0)
+            if not seen:
+                raise ValueError("the model never called skip_hook (no encoder layer?)")
             slot.skip = seen[-1]  # the tensor the capture recorded (the graph rewrites it in place)
             slot.skip_ready = ev
             if (slot.static_output.dim() != 3 or slot.skip.shape[:2] != slot.static_output.shape[:2]
